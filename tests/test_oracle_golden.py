@@ -1,0 +1,81 @@
+"""Pins the CPU oracle against golden vectors produced by the reference's own code
+(tests/golden/make_golden.py): store / load bit-exact, attention to fp32 round-off."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attn_oracle, kv_cache_oracle
+from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, attn_problem, bits, digest,
+                                load_problem, store_inputs)
+
+
+@pytest.fixture(scope="module")
+def store_golden(golden_dir):
+    return json.loads((golden_dir / "store_golden.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def load_golden(golden_dir):
+    return json.loads((golden_dir / "load_golden.json").read_text()), np.load(golden_dir / "load_written_rows.npz")
+
+
+@pytest.fixture(scope="module")
+def attn_golden(golden_dir):
+    return json.loads((golden_dir / "attn_golden.json").read_text()), np.load(golden_dir / "attn_golden.npz")
+
+
+@pytest.mark.parametrize("name", list(STORE_CASES))
+def test_store_oracle_matches_reference(name, store_golden):
+    key, value, k_cache, v_cache, slots = store_inputs(STORE_CASES[name])
+    g = store_golden[name]
+    assert digest(key.contiguous(), value.contiguous(), k_cache, v_cache, slots) == g["inputs"], "inputs drifted"
+    kc, vc = bits(k_cache).copy(), bits(v_cache).copy()
+    kv_cache_oracle.store_kvcache_unified(bits(key), bits(value), kc, vc, slots.numpy())
+    assert digest(kc) == g["k_cache"]
+    assert digest(vc) == g["v_cache"]
+
+
+@pytest.mark.parametrize("name", list(LOAD_CASES))
+def test_load_oracle_matches_reference_on_rows_it_writes(name, load_golden):
+    meta, rows = load_golden
+    p = load_problem(LOAD_CASES[name])
+    g = meta[name]
+    assert digest(p.k_cache, p.v_cache, p.k, p.v, p.block_tables, p.context_lens, p.seq_lens_ts) == g["inputs"]
+    k_out, v_out = kv_cache_oracle.load_kvcache(
+        bits(p.k_cache), bits(p.v_cache), p.block_tables.numpy(), p.context_lens.numpy(), p.seq_lens_ts.numpy(),
+        p.cu_seqlens_q.numpy(), p.cu_seqlens_k_total.numpy(), bits(p.k), bits(p.v))
+    written = np.unpackbits(rows[name])[: g["rows"]].astype(bool)
+    # the oracle's model of which rows the reference leaves unwritten agrees with what it did
+    model = kv_cache_oracle.reference_written_rows(
+        p.geometry.page_size, p.block_tables.numpy(), p.context_lens.numpy(), p.seq_lens_ts.numpy(),
+        p.cu_seqlens_k_total.numpy(), p.geometry.diffusion_block_size)
+    assert np.array_equal(model, written)
+    assert int(written.sum()) == g["rows_written"]
+    assert digest(k_out[written]) == g["k_written"]
+    assert digest(v_out[written]) == g["v_written"]
+
+
+@pytest.mark.parametrize("name", list(ATTN_CASES) + list(D2F_CASES))
+def test_attention_oracle_matches_reference(name, attn_golden):
+    meta, arrays = attn_golden
+    case = ATTN_CASES.get(name) or D2F_CASES[name]
+    p = attn_problem(case)
+    assert digest(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens) == meta[name]["inputs"]
+    o = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
+                                     p.cu_seqlens_q, p.cu_seqlens_k, p.scale, p.mask_mode,
+                                     p.geometry.diffusion_block_size)
+    want = torch.from_numpy(arrays[name])
+    torch.testing.assert_close(o[:, meta[name]["heads"]], want, atol=2e-5, rtol=1e-5)
+
+
+def test_attention_oracle_varlen_offsets():
+    """cu_seqlens_k cumulating ctx+new (varlen convention) gives the same result when the
+    in-flight rows are addressed through cu_seqlens_q."""
+    p = attn_problem(ATTN_CASES["ragged_q"])
+    a = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
+                                     p.cu_seqlens_q, p.cu_seqlens_k, p.scale)
+    b = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
+                                     p.cu_seqlens_q, p.cu_seqlens_k_total, p.scale, kv_offsets_from_q=True)
+    assert torch.equal(a, b)
