@@ -1,0 +1,35 @@
+// Device-side argument block and launch plans shared by the decode-attention kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dlx {
+
+struct DecodeArgs {
+    const void *q, *k, *v, *k_cache, *v_cache;
+    void* out;
+    const int32_t *block_tables, *context_lens, *cu_q, *cu_kv;  // cu_kv == nullptr: in-flight rows follow cu_q
+    float* ws_o;    // [num_splits, total_q, Hq, hd] normalised fp32 partial outputs
+    float* ws_lse;  // [num_splits, total_q, Hq]     log2-sum-exp of each partial (-inf: nothing seen)
+    int64_t q_rs, k_rs, v_rs, o_rs;     // row strides, elements
+    int64_t page_stride, token_stride;  // cache strides, elements
+    int64_t bt_stride, num_pages;
+    int total_q, num_seqs, max_blocks, max_q_len;
+    int hq, hkv, group, page_size;
+    int mask_mode, dbs;
+    int num_splits, m_blocks;
+    float scale_log2;  // softmax scale * log2(e)
+};
+
+// Tile plan of the mma.sync kernel for `rows` = G * max_q_len packed query rows.
+struct MmaPlan {
+    int id;
+    int block_m, block_n;
+    int m_blocks;
+    int ctas_per_sm;
+};
+MmaPlan plan_mma(int rows, int head_dim);
+int launch_decode_mma(const DecodeArgs& a, const MmaPlan& plan, int head_dim, cudaStream_t st);
+int launch_combine(const DecodeArgs& a, int head_dim, cudaStream_t st);
+
+}  // namespace dlx

@@ -1,0 +1,175 @@
+"""Tensor-level operators over the C ABI, registered as torch custom ops (namespace ``dlx_b200``).
+
+Each op only reads ``data_ptr()`` / strides / sizes, launches on ``torch.cuda.current_stream()`` and
+never synchronises, so all of them can be captured into a CUDA graph (the reference's
+block-diffusion runner captures the whole forward, diffulex/strategy/block_diffusion/engine/
+model_runner.py:206-274).  Outputs and the split-K workspace come from torch's caching allocator.
+CPU tensors are rejected: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import DecodeAttnParams, DlxError, check
+
+_DTYPES = {torch.bfloat16: _lib.DLX_DTYPE_BF16}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("diffulex_b200 operators run on CUDA tensors only (no CPU fallback)")
+
+
+# ---- store -------------------------------------------------------------------------------------
+@torch.library.custom_op("dlx_b200::store_kvcache_unified", mutates_args=("k_cache", "v_cache"))
+def store_kvcache_unified(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                          slot_mapping: torch.Tensor) -> None:
+    _need_cuda(key, value, k_cache, v_cache, slot_mapping)
+    n, heads, hd = key.shape
+    d = heads * hd
+    if slot_mapping.dtype not in (torch.int32, torch.int64):
+        raise ValueError("slot_mapping must be int32 or int64")
+    if not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.contiguous()
+    num_slots = k_cache.numel() // d
+    check(_lib.lib().dlx_store_kvcache_unified(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+        slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), n, d, key.element_size(), num_slots,
+        _stream()))
+
+
+@torch.library.custom_op("dlx_b200::store_kvcache_distinct", mutates_args=("k_cache", "v_cache"))
+def store_kvcache_distinct(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           slot_mapping: torch.Tensor) -> None:
+    _need_cuda(key, value, k_cache, v_cache, slot_mapping)
+    nb, heads, hd_x, page, x = k_cache.shape
+    if not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.contiguous()
+    check(_lib.lib().dlx_store_kvcache_distinct(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+        slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), key.shape[0], heads, hd_x * x, page, x, nb,
+        key.element_size(), _stream()))
+
+
+# ---- load --------------------------------------------------------------------------------------
+@torch.library.custom_op("dlx_b200::load_kvcache", mutates_args=())
+def load_kvcache(k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                 context_lens: torch.Tensor, seq_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                 cu_seqlens_k: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                 total_rows: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    _need_cuda(k_cache, v_cache, block_tables, context_lens, seq_lens, cu_seqlens_q, cu_seqlens_k, k_new, v_new)
+    nb, page, heads, hd = k_cache.shape
+    d = heads * hd
+    k_out = torch.empty((total_rows, heads, hd), device=k_cache.device, dtype=k_cache.dtype)
+    v_out = torch.empty_like(k_out)
+    i32 = lambda t: t if (t.dtype == torch.int32 and t.is_contiguous()) else t.to(torch.int32).contiguous()
+    bt, ctx, sl, cq, ck = map(i32, (block_tables, context_lens, seq_lens, cu_seqlens_q, cu_seqlens_k))
+    check(_lib.lib().dlx_load_kvcache(
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1),
+        k_new.data_ptr(), k_new.stride(0), v_new.data_ptr(), v_new.stride(0),
+        bt.data_ptr(), bt.stride(0), bt.shape[1], ctx.data_ptr(), sl.data_ptr(), cq.data_ptr(), ck.data_ptr(),
+        k_out.data_ptr(), v_out.data_ptr(), total_rows, bt.shape[0], page, nb, d, k_cache.element_size(), _stream()))
+    return k_out, v_out
+
+
+@load_kvcache.register_fake
+def _(k_cache, v_cache, block_tables, context_lens, seq_lens, cu_seqlens_q, cu_seqlens_k, k_new, v_new, total_rows):
+    shape = (total_rows, k_cache.shape[2], k_cache.shape[3])
+    return k_cache.new_empty(shape), k_cache.new_empty(shape)
+
+
+# ---- decode attention --------------------------------------------------------------------------
+def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
+                   scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits) -> DecodeAttnParams:
+    if q.dtype not in _DTYPES:
+        raise ValueError(f"decode attention is built for bf16, got {q.dtype}")
+    total_q, hq, hd = q.shape
+    hkv = k.shape[1]
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.stride(-1) != 1 or t.stride(1) != hd:
+            raise ValueError(f"{name}: heads must be contiguous ([tokens, heads, head_dim] with head stride head_dim)")
+    p = DecodeAttnParams()
+    p.struct_bytes = ctypes.sizeof(DecodeAttnParams)
+    p.dtype = _DTYPES[q.dtype]
+    p.q, p.k, p.v, p.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    p.q_row_stride, p.k_row_stride, p.v_row_stride, p.out_row_stride = q.stride(0), k.stride(0), v.stride(0), out.stride(0)
+    if k_cache is not None and k_cache.numel() > 0:
+        if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+            raise ValueError("k_cache and v_cache must share shape and strides")
+        if k_cache.stride(3) != 1 or k_cache.stride(2) != hd:
+            raise ValueError("cache must be [pages, page_size, Hkv, head_dim] with contiguous heads")
+        p.k_cache, p.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+        p.cache_page_stride, p.cache_token_stride = k_cache.stride(0), k_cache.stride(1)
+        p.num_pages, p.page_size = k_cache.shape[0], k_cache.shape[1]
+        p.block_tables = block_tables.data_ptr()
+        p.block_table_stride = block_tables.stride(0)
+        p.max_blocks = block_tables.shape[1]
+    else:
+        p.num_pages, p.page_size, p.max_blocks = 0, 1, 0
+    p.context_lens = context_lens.data_ptr()
+    p.cu_seqlens_q = cu_seqlens_q.data_ptr()
+    p.cu_seqlens_kv = cu_seqlens_kv.data_ptr() if cu_seqlens_kv is not None else None
+    p.total_q, p.num_seqs = total_q, cu_seqlens_q.numel() - 1
+    p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
+    p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
+    p.mask_mode, p.diffusion_block_size = mask_mode, diffusion_block_size
+    p.num_splits, p.kernel = num_splits, 0
+    p.scale = scale
+    return p
+
+
+@torch.library.custom_op("dlx_b200::decode_attn", mutates_args=())
+def decode_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                cu_seqlens_kv: Optional[torch.Tensor], scale: float, max_q_len: int, max_kv_len: int,
+                mask_mode: int, diffusion_block_size: int, num_splits: int) -> torch.Tensor:
+    _need_cuda(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv)
+    for name, t in (("block_tables", block_tables), ("context_lens", context_lens), ("cu_seqlens_q", cu_seqlens_q),
+                    ("cu_seqlens_kv", cu_seqlens_kv)):
+        if t is not None and t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block_tables must be [num_seqs, max_blocks] with contiguous rows")
+    out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), device=q.device, dtype=q.dtype)
+    p = _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
+                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
+    handle = _lib.lib()
+    ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
+    if ws_bytes < 0:
+        check(int(-ws_bytes))
+    ws = None
+    if ws_bytes > 0:
+        ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws_bytes
+    check(handle.dlx_decode_attn(ctypes.byref(p), _stream()))
+    return out
+
+
+@decode_attn.register_fake
+def _(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale, max_q_len,
+      max_kv_len, mask_mode, diffusion_block_size, num_splits):
+    return q.new_empty(q.shape)
+
+
+def planned_num_splits(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                       max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits) -> int:
+    """How many key-range splits a decode call with these arguments uses (host-side planning only)."""
+    p = _decode_params(q, k, v, k_cache, v_cache, q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                       max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
+    n = _lib.lib().dlx_decode_attn_num_splits(ctypes.byref(p))
+    if n < 0:
+        check(-n)
+    return n
+
+
+__all__ = ["store_kvcache_unified", "store_kvcache_distinct", "load_kvcache", "decode_attn", "planned_num_splits",
+           "DlxError"]

@@ -1,0 +1,150 @@
+/*
+ * dlx_b200.h - C ABI of the B200 (sm_100a) kernels for Diffulex's decode hot path.
+ *
+ * Three operators, each the device body of one Python entry point of the reference's
+ * diffulex_kernel package:
+ *
+ *   dlx_store_kvcache_unified  <- store_kvcache_unified_layout
+ *                                 (diffulex_kernel/python/kv_cache_kernels.py:110-124, kernel :11-32)
+ *   dlx_load_kvcache           <- load_kvcache (kv_cache_kernels.py:230-279, kernel :127-227)
+ *   dlx_decode_attn            <- dllm_flash_attn_decode
+ *                                 (diffulex_kernel/python/dllm_flash_attn.py:599-637, kernels :163-536)
+ *   dlx_store_kvcache_distinct <- store_kvcache_distinct_layout (kv_cache_kernels.py:86-107, kernel :35-83)
+ *
+ * Conventions: every pointer is a DEVICE pointer unless stated; strides are in ELEMENTS; all
+ * functions only enqueue work on `stream` (a cudaStream_t passed as void*), never synchronise,
+ * never allocate, never throw; they return 0 or a dlx_status code and leave a message retrievable
+ * with dlx_last_error() (thread local).  Nothing is retained after return.  All launches are
+ * legal inside CUDA stream capture.
+ */
+#ifndef DLX_B200_H
+#define DLX_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    DLX_OK = 0,
+    DLX_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, inconsistent counts            */
+    DLX_ERR_UNSUPPORTED = 2,      /* geometry or dtype with no kernel (e.g. head_dim not 64/128) */
+    DLX_ERR_ALIGNMENT = 3,        /* a base pointer or stride breaks the 16-byte vector rule     */
+    DLX_ERR_WORKSPACE = 4,        /* split-K workspace missing or too small                      */
+    DLX_ERR_CUDA = 5              /* a CUDA runtime call failed; see dlx_last_error()            */
+} dlx_status;
+
+enum { DLX_DTYPE_BF16 = 0, DLX_DTYPE_FP16 = 1 };
+
+/* Which keys a query row sees.  Cached keys (positions < context_len) are always visible.
+ * FULL: every in-flight key (the static block-diffusion kernel, dllm_flash_attn.py:300-307, and
+ *       the non-causal varlen call, :634-637).
+ * BLOCK_CAUSAL: in-flight key j is visible to query row i iff j < (i / dbs + 1) * dbs
+ *       (diffulex_legacy/engine/sequence.py:477-490; dllm_flash_attn.py:109-116). */
+enum { DLX_MASK_FULL = 0, DLX_MASK_BLOCK_CAUSAL = 1 };
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int dlx_version(void);
+const char* dlx_status_string(int status);
+/* Message of the last non-zero status returned on the calling thread ("" if none). */
+const char* dlx_last_error(void);
+
+/*
+ * Slot-mapped KV store, unified layout.  For every token t in [0, num_tokens) with
+ * slot[t] >= 0:  k_cache_rows[slot[t]] = key[t],  v_cache_rows[slot[t]] = value[t], where a cache
+ * row is `row_elems` = Hkv*head_dim contiguous elements and caches are [num_slots, row_elems].
+ * Tokens with slot < 0 are skipped (kv_cache_kernels.py:24-25).  Slots >= num_slots are skipped
+ * too (the reference would write out of bounds).  Offsets are 64-bit (the reference multiplies
+ * slot * D in int32, :30).  Bit-exact copy.
+ *   key/value       [num_tokens rows, row stride key_row_stride/value_row_stride elements]
+ *   slot_mapping    int32 (slot_is_int64 == 0) or int64 (!= 0), num_tokens entries
+ *   elem_bytes      size of one element (2 for bf16/fp16)
+ */
+int dlx_store_kvcache_unified(const void* key, int64_t key_row_stride, const void* value, int64_t value_row_stride,
+                              void* k_cache, void* v_cache, const void* slot_mapping, int slot_is_int64,
+                              int64_t num_tokens, int64_t row_elems, int elem_bytes, int64_t num_slots,
+                              void* stream);
+
+/*
+ * Slot-mapped KV store, split ("distinct") layout: K cache [NB, H, hd/x, PAGE, x],
+ * V cache [NB, H, hd, PAGE], both contiguous (kv_cache_kernels.py:35-107).
+ */
+int dlx_store_kvcache_distinct(const void* key, int64_t key_row_stride, const void* value, int64_t value_row_stride,
+                               void* k_cache, void* v_cache, const void* slot_mapping, int slot_is_int64,
+                               int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                               int32_t x, int64_t num_pages, int elem_bytes, void* stream);
+
+/*
+ * Paged KV gather.  For sequence s (rows o = cu_seqlens_k[s] ...):
+ *   out[o + p]         = cache[block_tables[s][p / page] , p % page]   for p < context_lens[s]
+ *   out[o + ctx + j]   = kv_new[cu_seqlens_q[s] + j]                   for j < seq_lens[s]
+ * cu_seqlens_k cumulates ctx+new (kv_cache_kernels.py:245-248).  Writes every such row, including
+ * the last full page of a page-aligned context and a ragged in-flight tail, which the reference
+ * kernel leaves unwritten (:167, :204).  Bit-exact copy.  out_rows = rows of k_out/v_out;
+ * rows >= cu_seqlens_k[num_seqs] are left untouched.
+ *   cache_page_stride / cache_token_stride: elements between pages / between tokens of a page
+ *   block_tables [num_seqs, max_blocks] int32, row stride block_table_stride; -1 padded
+ */
+int dlx_load_kvcache(const void* k_cache, const void* v_cache, int64_t cache_page_stride, int64_t cache_token_stride,
+                     const void* k_new, int64_t k_new_row_stride, const void* v_new, int64_t v_new_row_stride,
+                     const int32_t* block_tables, int64_t block_table_stride, int32_t max_blocks,
+                     const int32_t* context_lens, const int32_t* seq_lens, const int32_t* cu_seqlens_q,
+                     const int32_t* cu_seqlens_k, void* k_out, void* v_out, int64_t out_rows, int32_t num_seqs,
+                     int32_t page_size, int64_t num_pages, int64_t row_elems, int elem_bytes, void* stream);
+
+/*
+ * Paged block-diffusion decode attention.  For sequence s, query rows
+ * q[cu_seqlens_q[s] .. cu_seqlens_q[s+1]) of every query head attend to
+ * [cached keys 0..context_lens[s]-1 (through block_tables) ; in-flight keys k/v[kv0 .. kv0+new)]
+ * with  out = softmax(scale * q k^T + mask) v,  fp32 accumulation, output in the input dtype.
+ * kv0/new come from cu_seqlens_kv (which cumulates IN-FLIGHT lengths only, the static decode
+ * convention, diffulex/strategy/block_diffusion/engine/model_runner.py:135-139); pass
+ * cu_seqlens_kv == NULL to address the in-flight rows with cu_seqlens_q (varlen convention, where
+ * the caller's cu_seqlens_k cumulates ctx+new).  Query head h reads KV head h / (Hq/Hkv)
+ * (dllm_flash_attn.py:236).  Sequences with a non-positive query length are skipped.
+ */
+typedef struct dlx_decode_attn_params {
+    uint32_t struct_bytes;       /* = sizeof(dlx_decode_attn_params), checked                          */
+    int32_t dtype;               /* DLX_DTYPE_BF16 | DLX_DTYPE_FP16                                    */
+    const void* q;               /* [total_q, Hq, hd], head stride hd, row stride q_row_stride         */
+    const void* k;               /* [total_kv_new, Hkv, hd]                                            */
+    const void* v;
+    const void* k_cache;         /* [num_pages, page_size, Hkv, hd], head stride hd                    */
+    const void* v_cache;
+    void* out;                   /* [total_q, Hq, hd], row stride out_row_stride                       */
+    const int32_t* block_tables; /* [num_seqs, max_blocks], -1 padded                                  */
+    const int32_t* context_lens; /* [num_seqs]                                                         */
+    const int32_t* cu_seqlens_q; /* [num_seqs + 1]                                                     */
+    const int32_t* cu_seqlens_kv;/* [num_seqs + 1] in-flight offsets, or NULL (= cu_seqlens_q)         */
+    void* workspace;             /* split-K scratch, >= dlx_decode_attn_workspace_bytes(); may be NULL
+                                    when that returns 0                                                */
+    int64_t workspace_bytes;
+    int64_t q_row_stride, k_row_stride, v_row_stride, out_row_stride;
+    int64_t cache_page_stride, cache_token_stride;
+    int64_t block_table_stride;
+    int64_t num_pages;
+    int32_t total_q;             /* rows of q / out                                                    */
+    int32_t num_seqs, max_blocks;
+    int32_t num_q_heads, num_kv_heads, head_dim, page_size;
+    int32_t max_q_len;           /* host upper bound on rows per sequence (sizes the M tile)           */
+    int32_t max_kv_len;          /* host upper bound on ctx+new per sequence; 0 = max_blocks*page_size
+                                    + max_q_len.  Only steers the split-K choice                       */
+    int32_t mask_mode;           /* DLX_MASK_*                                                         */
+    int32_t diffusion_block_size;
+    int32_t num_splits;          /* 0 = choose; >= 1 forces that many key-range splits per sequence    */
+    int32_t kernel;              /* 0 = choose; 1 = mma.sync kernel; 2 = tcgen05 kernel (if eligible)   */
+    float scale;                 /* softmax scale, hd^-1/2 in every shipped model                      */
+} dlx_decode_attn_params;
+
+/* Bytes of scratch dlx_decode_attn needs for these parameters (0 when no split is used), or a
+ * negative dlx_status.  Depends only on host-known sizes, never on device contents. */
+int64_t dlx_decode_attn_workspace_bytes(const dlx_decode_attn_params* p);
+/* Number of splits dlx_decode_attn will use for these parameters. */
+int32_t dlx_decode_attn_num_splits(const dlx_decode_attn_params* p);
+int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DLX_B200_H */

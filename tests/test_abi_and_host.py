@@ -1,0 +1,230 @@
+"""CPU-only checks: the C-ABI library builds, loads and exports every symbol the header declares;
+argument validation and split planning (host code, no launch); the Python mirror's error
+behaviour; the data-parallel partition and gather (gloo, world_size 2)."""
+import ctypes
+import os
+import re
+import socket
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from diffulex_b200 import _lib
+    from diffulex_b200.build import build
+    build()
+    return _lib.lib()
+
+
+def good_params(**over):
+    from diffulex_b200._lib import DecodeAttnParams
+    p = DecodeAttnParams()
+    p.struct_bytes = ctypes.sizeof(DecodeAttnParams)
+    p.total_q, p.num_seqs, p.max_blocks = 2048, 64, 9
+    p.num_q_heads, p.num_kv_heads, p.head_dim, p.page_size = 28, 4, 128, 256
+    p.max_q_len, p.max_kv_len, p.mask_mode, p.diffusion_block_size = 32, 0, 0, 32
+    p.scale = 128 ** -0.5
+    for k, v in over.items():
+        setattr(p, k, v)
+    return p
+
+
+def test_header_symbols_are_exported(lib):
+    header = (ROOT / "include" / "dlx_b200.h").read_text()
+    declared = set(re.findall(r"\b(dlx_[a-z0-9_]+)\s*\(", header))
+    assert {"dlx_store_kvcache_unified", "dlx_load_kvcache", "dlx_decode_attn"} <= declared
+    from diffulex_b200._lib import EXPORTED_SYMBOLS
+    assert declared == set(EXPORTED_SYMBOLS), "ctypes binding and header disagree"
+    for name in declared:
+        assert getattr(lib, name) is not None
+    assert lib.dlx_version() >= 100
+    assert lib.dlx_status_string(0) == b"ok"
+
+
+def test_decode_validation_statuses(lib):
+    from diffulex_b200._lib import DecodeAttnParams
+    ws = lambda p: lib.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
+    assert ws(good_params()) >= 0
+    assert ws(good_params(struct_bytes=8)) == -1
+    assert b"struct_bytes" in lib.dlx_last_error()
+    assert ws(good_params(head_dim=96)) == -2
+    assert ws(good_params(num_kv_heads=5)) == -1
+    assert ws(good_params(mask_mode=7)) == -1
+    assert ws(good_params(mask_mode=1, diffusion_block_size=0)) == -1
+    assert ws(good_params(scale=0.0)) == -1
+    assert ws(good_params(dtype=1)) == -2
+    # null data pointers are refused before anything is launched
+    assert lib.dlx_decode_attn(ctypes.byref(good_params()), None) == 1
+    assert lib.dlx_decode_attn(None, None) == 1
+    # an empty batch is a no-op
+    assert lib.dlx_decode_attn(ctypes.byref(good_params(num_seqs=0, total_q=0)), None) == 0
+
+
+def test_store_and_load_validation_statuses(lib):
+    assert lib.dlx_store_kvcache_unified(None, 512, None, 512, None, None, None, 0, 0, 512, 2, 10, None) == 0
+    assert lib.dlx_store_kvcache_unified(None, 512, None, 512, None, None, None, 0, 4, 512, 2, 10, None) == 1
+    assert lib.dlx_store_kvcache_unified(None, 512, None, 512, None, None, None, 0, -1, 512, 2, 10, None) == 1
+    buf = ctypes.create_string_buffer(64)
+    a = ctypes.addressof(buf)
+    # row stride smaller than a row
+    assert lib.dlx_store_kvcache_unified(a, 256, a, 512, a, a, a, 0, 4, 512, 2, 10, None) == 1
+    assert lib.dlx_load_kvcache(None, None, 0, 0, None, 0, None, 0, None, 0, 0, None, None, None, None, None, None,
+                                0, 0, 256, 0, 512, 2, None) == 0
+    assert lib.dlx_load_kvcache(None, None, 0, 0, None, 0, None, 0, None, 0, 1, None, None, None, None, None, None,
+                                10, 2, 256, 4, 512, 2, None) == 1
+    assert lib.dlx_store_kvcache_distinct(a, 512, a, 512, a, a, a, 0, 4, 4, 128, 256, 7, 4, 2, None) == 1
+
+
+def test_split_planning_is_host_only_and_sized_right(lib):
+    n = lambda p: lib.dlx_decode_attn_num_splits(ctypes.byref(p))
+    ws = lambda p: lib.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
+    # 64 seqs x 4 KV heads = 256 CTAs >= 148 slots, contexts <= 2336 keys: one pass, no scratch
+    p = good_params()
+    assert n(p) == 1 and ws(p) == 0
+    # forced splits: lse [splits, rows] (256-byte padded) + partial O [splits, rows, hd] fp32
+    p = good_params(num_splits=3)
+    rows = 2048 * 28
+    assert n(p) == 3 and ws(p) == ((3 * rows * 4 + 255) // 256) * 256 + 3 * rows * 128 * 4
+    # few sequences: split to fill 148 SMs
+    p = good_params(num_seqs=2, total_q=64)
+    assert n(p) > 1
+    # very long contexts are cut even when CTAs abound
+    p = good_params(num_seqs=256, total_q=8192, max_blocks=129)
+    assert n(p) >= 3
+
+
+def test_python_mirror_rejects_bad_inputs_without_a_gpu(lib):
+    import diffulex_b200 as dlx
+    from diffulex_b200.workload import make_problem, small_workload
+    p = make_problem(small_workload("t", 8, 2, 64, 16, 4, [10, 3], [4, 4]), device="cpu")
+    md = p.metadata("static")
+    with pytest.raises(AssertionError):
+        dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, p.slot_mapping[:-1], md)
+    with pytest.raises(AssertionError):
+        dlx.store_kvcache_unified_layout(p.k.transpose(1, 2), p.v, p.k_cache, p.v_cache, p.slot_mapping, md)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, p.slot_mapping, md)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+    md.decode_mode = "other"
+    with pytest.raises(ValueError):
+        dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+    with pytest.raises(NotImplementedError):
+        dlx.dllm_flash_attn_prefill(p.q, p.k, p.v, p.scale, md)
+
+
+def test_missing_library_is_an_import_error(tmp_path, monkeypatch):
+    from diffulex_b200 import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libdlx_b200.so")
+    with pytest.raises(ImportError, match="no CPU or PyTorch fallback"):
+        _lib.lib()
+
+
+def test_dropin_package_exposes_reference_names(lib, monkeypatch):
+    import importlib
+    import sys
+    monkeypatch.syspath_prepend(str(ROOT / "diffulex_b200" / "dropin"))
+    for m in [k for k in sys.modules if k.startswith("diffulex_kernel")]:
+        monkeypatch.delitem(sys.modules, m)
+    mod = importlib.import_module("diffulex_kernel")
+    for name in ("store_kvcache_distinct_layout", "store_kvcache_unified_layout", "dllm_flash_attn_decode",
+                 "dllm_flash_attn_prefill"):
+        assert callable(getattr(mod, name))
+    sub = importlib.import_module("diffulex_kernel.python.kv_cache_kernels")
+    assert callable(sub.load_kvcache)
+
+
+# ---- workloads and partition ---------------------------------------------------------------------
+def test_named_workloads_match_the_benchmark_configurations():
+    from diffulex_b200.workload import named_workload
+    w = named_workload("cfg2")
+    assert len(w.context_lens) == 64 and w.context_lens.min() >= 512 and w.context_lens.max() <= 2048
+    assert (w.geometry.num_q_heads, w.geometry.num_kv_heads, w.geometry.head_dim, w.geometry.layers) == (28, 4, 128, 28)
+    w = named_workload("cfg3")
+    assert (w.new_lens == 128).all() and w.mask_mode == 1 and w.geometry.num_kv_heads == 32
+    w = named_workload("cfg4")
+    assert w.context_lens.min() >= 128 and w.context_lens.max() <= 8192 and (w.new_lens == 4).all()
+    w = named_workload("cfg5")
+    assert len(w.context_lens) == 256 and w.context_lens.min() >= 4096 and w.context_lens.max() <= 32768
+    assert np.array_equal(named_workload("cfg5").context_lens, w.context_lens), "seeded"
+
+
+def test_lpt_partition_is_exact_and_balanced():
+    from diffulex_b200.workload import named_workload, partition_lpt, shard_workload
+    w = named_workload("cfg5")
+    costs = (w.context_lens + w.new_lens).tolist()
+    for ws in (2, 4, 8):
+        parts = partition_lpt(costs, ws)
+        assert sorted(sum(parts, [])) == list(range(len(costs)))
+        loads = [sum(costs[i] for i in p) for p in parts]
+        assert max(loads) / (sum(loads) / ws) < 1.01
+        sub, owned = shard_workload(w, 1, ws)
+        assert owned == parts[1] and np.array_equal(sub.context_lens, w.context_lens[owned])
+
+
+def test_page_tables_are_disjoint_permuted_and_padded():
+    from diffulex_b200.workload import make_problem, named_workload
+    p = make_problem(named_workload("cfg1"), device="cpu")
+    bt = p.block_tables.numpy()
+    used = bt[bt >= 0]
+    assert len(set(used.tolist())) == len(used) and (bt == -1).any()
+    assert used.max() < p.k_cache.shape[0]
+    assert not np.array_equal(np.sort(used), used), "physical pages are not handed out in order"
+    # slots of the in-flight rows land in the right page at the right offset
+    s, pos = 2, int(p.host_context_lens[2]) + 5
+    slot = int(p.slot_mapping[int(p.cu_seqlens_q[2]) + 5])
+    assert slot == bt[s, pos // 256] * 256 + pos % 256
+
+
+# ---- data-parallel gather over gloo ----------------------------------------------------------------
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _dp_worker(rank, world_size, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    try:
+        from diffulex_b200 import dp
+        from diffulex_b200.workload import partition_lpt
+        q_lens = [3, 5, 2, 7, 1, 4]
+        costs = [100, 900, 50, 700, 20, 300]
+        parts = partition_lpt(costs, world_size)
+        cu = np.concatenate([[0], np.cumsum(q_lens)])
+        # a rank's "attention output": row value = global query row index
+        rows = np.concatenate([np.arange(cu[s], cu[s + 1]) for s in parts[rank]])
+        local = torch.from_numpy(rows).float().view(-1, 1, 1).expand(-1, 2, 3).contiguous()
+        full = dp.gather_outputs(local, parts, q_lens)
+        ok = torch.equal(full[:, 0, 0], torch.arange(int(cu[-1])).float()) and full.shape == (int(cu[-1]), 2, 3)
+        t = dp.max_over_ranks(1.0 + rank)
+        ts = dp.gather_timings(1.0 + rank)
+        tot = dp.sum_over_ranks(10.0)
+        q.put((rank, bool(ok), t, ts, tot))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_gather_world_size_2_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok, t, ts, tot in results:
+        assert ok and t == 2.0 and ts == [1.0, 2.0] and tot == 20.0
