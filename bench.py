@@ -1,0 +1,345 @@
+#!/usr/bin/env python
+"""Benchmark of the decode hot path: per layer, slot-mapped KV store of the in-flight block and
+paged block-diffusion decode attention, over all layers of the model shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2] [--impl ours|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N ... bench.py --gpus N ...
+
+One JSON line on rank 0.  ``value`` is the attention's algorithmic KV-read rate, summed over ranks:
+(valid cached + in-flight tokens) x 2 x Hkv x hd x 2 B per layer call, each byte counted once.
+
+* a step = L layers x (store + decode), L distinct caches (4.8 GB for cfg2, far above the 126 MB
+  L2, so nothing is reused between layer calls or steps);
+* ``value``: the step is captured once into a CUDA graph (the reference's block-diffusion runner
+  replays its decode step the same way) and K replays are timed with CUDA events between
+  barriers; inputs are resident in HBM;
+* ``e2e``: the same step through the Python entry points with HOST inputs: q/k/v and all
+  metadata copied from pinned memory, outputs copied back, every step, inside the timed region;
+* ``roofline``: the decode kernel alone, every launch bracketed by CUDA events on its stream
+  (eager launches, same caches), against the measured HBM copy bandwidth;
+* ``cpu_baseline`` / ``--impl reference``: the PyTorch fp32 CPU restatement of the reference's
+  attention check (oracle/attn_oracle.py) on the host cores, on a bounded sample (one layer).
+
+N > 1 is weak scaling: every rank runs its own batch of the workload (rank-specific seed) on its own
+GPU with no data-path collective; NCCL only reduces timings.  ``--scaling strong`` instead shards
+one global batch by sequences (LPT on KV tokens).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np
+import torch
+
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per decode launch from the committed ncu captures
+# (profiles/), keyed by workload; None until a capture exists for that workload.
+NCU_TRAFFIC_BYTES = {}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = the model's)")
+    ap.add_argument("--num-splits", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled while the timed region runs."""
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.rows, self.proc = [], None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), line.strip()))
+
+    def window(self, t0, t1):
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ts, line in self.rows:
+            if ts < t0 - 0.15 or ts > t1 + 0.15:
+                continue
+            parts = [x.strip() for x in line.split(",")]
+            try:
+                sm.append(float(parts[0])); smax = max(smax, float(parts[1]))
+            except Exception:
+                continue
+            for n, v in zip(names, parts[2:]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+
+
+def cpu_attention_baseline(w, budget_s=12.0):
+    """Oracle port on the host cores: one layer of the workload (all sequences), repeated within a
+    time budget.  Returns (GB/s of bf16-equivalent KV, query tok/s, cores, sample description)."""
+    from diffulex_b200.workload import make_problem
+    from oracle import attn_oracle
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    p = make_problem(w, device="cpu", values="numpy")
+    f = lambda t: t.float()
+    args = (f(p.q), f(p.k), f(p.v), f(p.k_cache), f(p.v_cache), p.block_tables, p.context_lens, p.cu_seqlens_q,
+            p.cu_seqlens_k, p.scale, p.mask_mode, p.geometry.diffusion_block_size)
+    attn_oracle.decode_attention(*args)  # warm-up
+    times, t_start = [], time.time()
+    while len(times) < 3 or (time.time() - t_start < budget_s and len(times) < 50):
+        t = time.time(); attn_oracle.decode_attention(*args); times.append(time.time() - t)
+    dt = statistics.median(times)
+    return (p.kv_bytes() / dt / 1e9, int(p.host_new_lens.sum()) / dt, cores,
+            f"1 of {w.geometry.layers} layers, all {p.num_seqs} sequences, fp32, {len(times)} runs, median")
+
+
+def run_reference(args, w, rank, world):
+    """The reference's CPU implementation of the path (its PyTorch attention check, restated in
+    oracle/attn_oracle.py; the reference itself is Python and cannot travel) on the host cores."""
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        pass  # warm-up happens inside cpu_attention_baseline
+    gbs, toks, cores, sample = cpu_attention_baseline(w, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
+    line = {
+        "impl": "reference", "metric": "decode_attn_kv_read_gbps", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "query_tokens_per_s": toks,
+        "config": {"workload": f"{w.name}: {w.note}", "sample": sample},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    from diffulex_b200.workload import make_problem, named_workload, shard_workload
+
+    w_global = named_workload(args.workload)
+    if args.impl == "reference":
+        run_reference(args, w_global, rank, world)
+        return
+
+    import torch.distributed as dist
+    assert torch.cuda.is_available(), "bench.py needs a CUDA device (there is no CPU fallback)"
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    import diffulex_b200 as dlx
+    from diffulex_b200 import dp, ops
+
+    # ---- this rank's batch ----
+    if args.scaling == "strong":
+        w, owned = shard_workload(w_global, rank, world)
+    else:
+        w = named_workload(args.workload, seed=w_global.seed + 100 * rank) if world > 1 else w_global
+    geo = w.geometry
+    L = args.layers or geo.layers
+    base = make_problem(w, device=dev, values="torch")
+    layers = [base]
+    gen = torch.Generator(device=dev); gen.manual_seed(w.seed + 1)
+    for _ in range(1, L):
+        rnd = lambda t: torch.empty_like(t).normal_(0, 1, generator=gen)
+        layers.append(type(base)(**{**{f: getattr(base, f) for f in base.__dataclass_fields__},
+                                    "q": rnd(base.q), "k": rnd(base.k), "v": rnd(base.v),
+                                    "k_cache": rnd(base.k_cache), "v_cache": rnd(base.v_cache)}))
+    md = base.metadata("static")
+    md.num_splits = args.num_splits
+    kv_bytes_layer = base.kv_bytes()
+    q_tokens = int(base.host_new_lens.sum())
+    flops_layer = base.flops()
+    splits = ops.planned_num_splits(base.q, base.k, base.v, base.k_cache, base.v_cache, base.block_tables,
+                                    base.context_lens, base.cu_seqlens_q, base.cu_seqlens_k, base.scale,
+                                    md.max_seqlen_q, 0, base.mask_mode, geo.diffusion_block_size, args.num_splits)
+    launches_per_layer = 2 + (1 if splits > 1 else 0)
+
+    def step(outs=None):
+        for i, p in enumerate(layers):
+            dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
+            o = dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+            if outs is not None:
+                outs[i] = o
+        return o
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: CUDA-graph replay of the step ----
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(); step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    time.sleep(0.25)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    barrier()
+    t_wall1 = time.time()
+    ms_local = e0.elapsed_time(e1)
+    ms_total = dp.max_over_ranks(ms_local, dev)
+    clocks = sampler.window(t_wall0, t_wall1) if sampler else None
+    total_kv_bytes = dp.sum_over_ranks(float(kv_bytes_layer) * L * args.steps, dev)
+    total_q_tokens = dp.sum_over_ranks(float(q_tokens) * args.steps, dev)
+    value = total_kv_bytes / (ms_total * 1e-3) / 1e9
+    per_rank_ms = dp.gather_timings(ms_local, dev)
+
+    # ---- roofline: the decode kernel alone, per-launch CUDA events (eager) ----
+    peak, peak_kind = peaks()
+    evs = []
+    for it in range(3 + min(args.steps, 10)):
+        for p in layers:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
+            a.record()
+            dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+            b.record()
+            if it >= 3:
+                evs.append((a, b))
+    torch.cuda.synchronize()
+    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    avg_launch_ms = sum(launch_ms) / len(launch_ms)
+    achieved = kv_bytes_layer / (avg_launch_ms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "decode attention (+ combine if split)",
+                "algorithmic_bytes_per_launch": kv_bytes_layer, "avg_launch_us": avg_launch_ms * 1e3,
+                "min_launch_us": min(launch_ms) * 1e3, "tflops": flops_layer / (avg_launch_ms * 1e-3) / 1e12}
+
+    # ---- e2e: host buffers in, host buffers out, every step ----
+    e2e = None
+    if not args.no_e2e:
+        pin = lambda t: t.cpu().pin_memory()
+        h_q = torch.stack([p.q for p in layers]).cpu().pin_memory()
+        h_k = torch.stack([p.k for p in layers]).cpu().pin_memory()
+        h_v = torch.stack([p.v for p in layers]).cpu().pin_memory()
+        h_meta = {n: pin(getattr(base, n)) for n in ("block_tables", "context_lens", "cu_seqlens_q", "cu_seqlens_k",
+                                                     "slot_mapping")}
+        h_out = torch.empty((L,) + tuple(base.q.shape), dtype=base.q.dtype).pin_memory()
+        d_q, d_k, d_v = (torch.empty_like(t, device=dev) for t in (h_q, h_k, h_v))
+        d_out = torch.empty_like(h_out, device=dev)
+        from types import SimpleNamespace
+        h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, *h_meta.values()))
+        d2h = h_out.numel() * h_out.element_size()
+
+        def e2e_step():
+            d_q.copy_(h_q, non_blocking=True); d_k.copy_(h_k, non_blocking=True); d_v.copy_(h_v, non_blocking=True)
+            m = SimpleNamespace(**vars(md))
+            for n, t in h_meta.items():
+                setattr(m, n, t.to(dev, non_blocking=True))
+            for i, p in enumerate(layers):
+                dlx.store_kvcache_unified_layout(d_k[i], d_v[i], p.k_cache, p.v_cache, m.slot_mapping, m)
+                d_out[i] = dlx.dllm_flash_attn_decode(d_q[i], d_k[i], d_v[i], p.k_cache, p.v_cache, p.scale, m)
+            h_out.copy_(d_out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()  # the caller holds the result on the host
+
+        for _ in range(max(3, min(args.warmup, 5))):
+            e2e_step()
+        barrier()
+        e0.record()
+        n_e2e = max(3, min(args.steps, 10))
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record()
+        barrier()
+        ms_e2e = dp.max_over_ranks(e0.elapsed_time(e1), dev)
+        tot = dp.sum_over_ranks(float(kv_bytes_layer) * L * n_e2e, dev)
+        e2e = {"value": tot / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e, "ms_per_step": ms_e2e / n_e2e}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, toks, cores, sample = cpu_attention_baseline(w_global)
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample,
+               "query_tokens_per_s": toks}
+    if sampler:
+        sampler.stop()
+
+    if rank == 0:
+        line = {
+            "metric": "decode_attn_kv_read_gbps", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_total / args.steps,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "query_tokens_per_s": total_q_tokens / (ms_total * 1e-3),
+            "config": {"workload": f"{w_global.name}: {w_global.note}", "layers": L, "seqs_per_gpu": base.num_seqs,
+                       "heads": f"{geo.num_q_heads}q/{geo.num_kv_heads}kv x {geo.head_dim}", "page_size": geo.page_size,
+                       "query_block": int(base.host_new_lens.max()), "kv_tokens_per_layer_per_gpu":
+                       int(base.host_context_lens.sum() + base.host_new_lens.sum()), "num_splits": splits,
+                       "step": "L x (store_kvcache_unified + decode attention), CUDA-graph replay",
+                       "l2": f"inputs larger than L2: {L} distinct layer caches, "
+                             f"{kv_bytes_layer * L / 1e9:.2f} GB of KV per step",
+                       "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.scaling})")},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps * L * launches_per_layer, "clocks": clocks, "per_rank_ms": per_rank_ms,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
