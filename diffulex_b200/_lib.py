@@ -56,6 +56,7 @@ _SIGNATURES = {
     "dlx_decode_attn_workspace_bytes": (c_int64, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn_num_splits": (c_int32, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
+    "dlx_debug_device_status": (c_int, [ctypes.POINTER(c_int32)]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

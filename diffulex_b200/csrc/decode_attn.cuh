@@ -32,4 +32,10 @@ MmaPlan plan_mma(int rows, int head_dim);
 int launch_decode_mma(const DecodeArgs& a, const MmaPlan& plan, int head_dim, cudaStream_t st);
 int launch_combine(const DecodeArgs& a, int head_dim, cudaStream_t st);
 
+// tcgen05 kernel: head_dim 128, 129..256 packed rows, bf16.
+bool tc5_eligible(int rows, int head_dim);
+int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st);
+// Copies out and clears the device status word of the tcgen05 kernel (synchronises the device).
+int read_tc5_status(int out[4]);
+
 }  // namespace dlx

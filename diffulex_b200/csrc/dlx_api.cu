@@ -15,6 +15,7 @@ char* last_error_buffer() {
 
 struct DecodePlan {
     MmaPlan mma;
+    bool use_tc5;
     int num_splits;
     int64_t ws_o_bytes, ws_lse_bytes;
 };
@@ -40,6 +41,10 @@ static int validate_decode(const dlx_decode_attn_params* p) {
         return fail(DLX_ERR_INVALID_ARGUMENT, "decode: block-causal mask needs diffusion_block_size > 0");
     if (p->num_splits < 0 || p->num_splits > 256) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: num_splits %d", p->num_splits);
     if (!(p->scale > 0.f) || !isfinite(p->scale)) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: scale must be positive and finite");
+    if (p->kernel < 0 || p->kernel > 2) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: kernel %d", p->kernel);
+    if (p->kernel == 2 && !tc5_eligible((int)((int64_t)(p->num_q_heads / p->num_kv_heads) * p->max_q_len > 1 << 20
+                                                  ? 1 << 20 : (p->num_q_heads / p->num_kv_heads) * p->max_q_len), p->head_dim))
+        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernel serves head_dim 128 with 129..256 packed rows");
     if (p->num_seqs > 65535) return fail(DLX_ERR_UNSUPPORTED, "decode: more than 65535 sequences per call");
     return DLX_OK;
 }
@@ -49,6 +54,10 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     const int group = p->num_q_heads / p->num_kv_heads;
     const int64_t rows = (int64_t)group * p->max_q_len;
     d.mma = plan_mma((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
+    d.use_tc5 = p->kernel != 1 && tc5_eligible((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
+    if (d.use_tc5) {  // one CTA per (sequence, KV head, split): 256 packed rows, 128-key tiles, 1 CTA/SM
+        d.mma.block_m = 256; d.mma.block_n = 128; d.mma.m_blocks = 1; d.mma.ctas_per_sm = 1;
+    }
     const int64_t max_len = p->max_kv_len > 0 ? p->max_kv_len : (int64_t)p->max_blocks * p->page_size + p->max_q_len;
     const int64_t max_tiles = (max_len + d.mma.block_n - 1) / d.mma.block_n;
     int splits = p->num_splits;
@@ -96,6 +105,15 @@ extern "C" const char* dlx_status_string(int status) {
 }
 
 extern "C" const char* dlx_last_error(void) { return last_error_buffer(); }
+
+extern "C" int dlx_debug_device_status(int32_t out[4]) {
+    if (out == nullptr) return fail(DLX_ERR_INVALID_ARGUMENT, "device_status: null output");
+    int tmp[4];
+    const int rc = read_tc5_status(tmp);
+    if (rc != DLX_OK) return rc;
+    for (int i = 0; i < 4; ++i) out[i] = tmp[i];
+    return DLX_OK;
+}
 
 extern "C" int64_t dlx_decode_attn_workspace_bytes(const dlx_decode_attn_params* p) {
     const int rc = validate_decode(p);
@@ -154,7 +172,7 @@ extern "C" int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream) {
         a.ws_o = reinterpret_cast<float*>(static_cast<char*>(p->workspace) + d.ws_lse_bytes);
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = launch_decode_mma(a, d.mma, hd, st);
+    rc = d.use_tc5 ? launch_decode_tc5(a, st) : launch_decode_mma(a, d.mma, hd, st);
     if (rc != DLX_OK) return rc;
     if (d.num_splits > 1) rc = launch_combine(a, hd, st);
     return rc;

@@ -9,6 +9,7 @@ CPU tensors are rejected: there is no fallback path.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -122,7 +123,7 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
     p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
     p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
     p.mask_mode, p.diffusion_block_size = mask_mode, diffusion_block_size
-    p.num_splits, p.kernel = num_splits, 0
+    p.num_splits, p.kernel = num_splits, int(os.environ.get("DLX_DECODE_KERNEL", "0"))  # 0 auto, 1 mma.sync, 2 tcgen05
     p.scale = scale
     return p
 

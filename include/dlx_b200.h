@@ -144,6 +144,14 @@ int64_t dlx_decode_attn_workspace_bytes(const dlx_decode_attn_params* p);
 int32_t dlx_decode_attn_num_splits(const dlx_decode_attn_params* p);
 int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream);
 
+/*
+ * Debug aid with no counterpart in the reference.  Every wait inside the tcgen05 kernel is bounded;
+ * a wait that runs out makes its CTA stop early and records {1, role, tile, cta} in a device status
+ * word instead of trapping.  This call synchronises the device, copies the word to the HOST array
+ * `out` and clears it.  out[0] == 0 means no wait ever expired.
+ */
+int dlx_debug_device_status(int32_t out[4]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -111,7 +111,11 @@ def test_load_bit_exact(name, dlx, golden_dir):
 @pytest.mark.parametrize("name", list(ATTN_CASES) + list(D2F_CASES))
 @pytest.mark.parametrize("mode", ["static", "varlen"])
 @pytest.mark.parametrize("num_splits", [0, 1, 3])
-def test_attention_matches_golden_and_oracle(name, mode, num_splits, dlx, golden_dir):
+@pytest.mark.parametrize("kernel", ["auto", "mma"])
+def test_attention_matches_golden_and_oracle(name, mode, num_splits, kernel, dlx, golden_dir, monkeypatch):
+    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128, 129..256 packed rows)
+    # and the mma.sync kernel elsewhere; "mma" forces the mma.sync kernel everywhere
+    monkeypatch.setenv("DLX_DECODE_KERNEL", {"auto": "0", "mma": "1"}[kernel])
     meta = json.loads((golden_dir / "attn_golden.json").read_text())[name]
     want_sel = torch.from_numpy(np.load(golden_dir / "attn_golden.npz")[name])
     p = attn_problem(ATTN_CASES.get(name) or D2F_CASES[name])
@@ -276,6 +280,23 @@ def test_cfg5_attention_properties(dlx, cfg5_problem):
         want = attn_oracle.decode_attention(pd.q[q0:q1].cpu(), pd.k[q0:q1].cpu(), pd.v[q0:q1].cpu(), kc, vc, bt,
                                             torch.tensor([ctx], dtype=torch.int32), cu, cu, pd.scale)
         torch.testing.assert_close(o_auto[q0:q1].float().cpu(), want, atol=ATOL, rtol=RTOL)
+
+
+def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
+    """Forcing the tcgen05 kernel works on an eligible shape (224 packed rows), is refused on an
+    ineligible one, and the kernel's bounded waits never ran out during this test session."""
+    import ctypes
+    from diffulex_b200 import _lib
+    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
+    p = attn_problem(ATTN_CASES["cfg1"])
+    for splits in (0, 2):
+        o = run_decode(dlx, to_dev(p), "static", splits)
+        torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)
+    with pytest.raises(_lib.DlxError):
+        run_decode(dlx, to_dev(attn_problem(ATTN_CASES["q4_gqa4"])))
+    st = (ctypes.c_int32 * 4)()
+    assert _lib.lib().dlx_debug_device_status(st) == 0
+    assert list(st) == [0, 0, 0, 0], f"a bounded wait expired: {list(st)}"
 
 
 # ---- error behaviour ---------------------------------------------------------------------------
