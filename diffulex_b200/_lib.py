@@ -57,6 +57,7 @@ _SIGNATURES = {
     "dlx_decode_attn_num_splits": (c_int32, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
     "dlx_debug_device_status": (c_int, [ctypes.POINTER(c_int32)]),
+    "dlx_debug_profile": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

@@ -37,5 +37,7 @@ bool tc5_eligible(int rows, int head_dim);
 int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st);
 // Copies out and clears the device status word of the tcgen05 kernel (synchronises the device).
 int read_tc5_status(int out[4]);
+// Cycle accounting of CTA (0,0,0) of the tcgen05 kernel: copy out (if out != null), clear, and switch on/off.
+int tc5_profile(int enable, unsigned long long out[16]);
 
 }  // namespace dlx

@@ -6,13 +6,15 @@
 // is fetched from HBM once and used by both: at ~224 flop per KV byte the legacy mma.sync pipe is
 // the limiter, the tcgen05 pipe is not.
 //
-// Warp roles (416 threads):
+// Warp roles (352 threads, up to 184 registers each so a softmax thread holds its whole S row):
 //   warps 0-3   softmax warpgroup of Q tile 0: thread <-> TMEM lane <-> query row
 //   warps 4-7   softmax warpgroup of Q tile 1
-//   warps 8-11  loaders: 16-byte cp.async of Q and of K/V tiles (128 keys) into 128B-swizzled
+//   warps 8-9   loaders: 16-byte cp.async of Q and of K/V tiles (128 keys) into 128B-swizzled
 //               shared memory (the canonical K-major / MN-major UMMA layouts), any page size, the
-//               cached prefix and the in-flight rows as ONE key axis, rows past the end zero-filled
-//   warp 12     one elected thread issues tcgen05.mma: S_t = Q_t K^T (SS form) into TMEM, and
+//               cached prefix and the in-flight rows as ONE key axis, rows past the end zero-filled;
+//               completion is signalled by cp.async.mbarrier.arrive, so loads run as far ahead as
+//               the two-stage K and V rings allow
+//   warp 10     one elected thread issues tcgen05.mma: S_t = Q_t K^T (SS form) into TMEM, and
 //               O_t += P_t V (TS form: P is read from TMEM, V^T from shared memory), and
 //               tcgen05.commit to the mbarriers that hand tiles back and forth
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 fp32 columns each; P_t (bf16) overwrites the first
@@ -39,16 +41,24 @@ constexpr int STAGES = 2;
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + STAGES * ITEM_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers/flags + slack for 1024-byte alignment
-constexpr int NUM_THREADS = 416;
-constexpr int LOADER_WARP0 = 8, MMA_WARP = 12;
-constexpr int NUM_LOADERS = 128;
+constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 2 stages x 128 rows
+constexpr int SMEM_BYTES = OFF_TAB + 4 * TILE_N * 8 + 1024;  // + slack for 1024-byte alignment
+constexpr int NUM_THREADS = 352;
+constexpr int LOADER_WARP0 = 8, MMA_WARP = 10;
+constexpr int NUM_LOADERS = 64;
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
 
 // barrier slots (8 bytes each) at OFF_BAR
 enum { B_QFULL = 0, B_KFULL = 1, B_VFULL = 3, B_KEMPTY = 5, B_VEMPTY = 7, B_SFULL = 9, B_PFULL = 11, B_OFULL = 13, B_COUNT = 14 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
+// Optional cycle accounting of CTA (0,0,0): [0] CTA lifetime, [role] cycles spent in that wait site,
+// [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
+__device__ unsigned long long g_prof[16];
+__device__ int g_prof_on;
+__device__ __forceinline__ bool prof_thread() {
+    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && ((threadIdx.x & 127) == 0 || threadIdx.x == 320);
+}
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
@@ -67,8 +77,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
+    const bool rec = prof_thread();
+    const long long c0 = rec ? clock64() : 0;
     for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
-        if (mbar_try(bar, parity)) return true;
+        if (mbar_try(bar, parity)) {
+            if (rec) atomicAdd(&g_prof[role], (unsigned long long)(clock64() - c0));
+            return true;
+        }
         if ((it & 255u) == 255u && *abort_flag) return false;
     }
     *abort_flag = 1;
@@ -83,6 +98,15 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_async_proxy() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
+// The mbarrier gets one arrival (of its expected count) once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
 }
@@ -209,6 +233,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const long long cta_c0 = (tid == 0 && prof_thread()) ? clock64() : 0;
 
     if (warp < 8) {
         // =========================== softmax warpgroups ===========================
@@ -230,21 +255,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
             tc_fence_after();
             if (warp_valid) {
                 const int key0 = (t0 + jj) * TILE_N;
-                const bool need_mask = key0 + TILE_N > full_until;
-                // pass 1: row maximum of the raw scores
-                float mx = -INFINITY;
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_ld_wait();
+                const bool rec = prof_thread();
+                long long c0 = rec ? clock64() : 0;
+                // the whole S row of this thread: 128 fp32 scores in registers, one TMEM round trip
+                uint32_t v[4][32];
+                tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
+                tmem_ld_wait();
+                if (key0 + TILE_N > full_until) {  // tile touches a mask boundary (warp-uniform)
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        float x = __uint_as_float(v[e]);
-                        if (need_mask && key0 + c * 32 + e >= limit) x = -INFINITY;
-                        mx = fmaxf(mx, x);
-                    }
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (key0 + c * 32 + e >= limit) v[c][e] = 0xff800000u;  // -inf
                 }
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2)
+                        mx = max3(mx, __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
+                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_new = fmaxf(m_used, mx * sl2);
                 const bool need = (m_new > m_used) && (m_used == -INFINITY || m_new - m_used > 8.f);
                 if (__any_sync(0xffffffffu, need)) {
@@ -252,39 +282,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
                     if (jj > 0) {  // O_t holds the sum over earlier tiles: rescale it in TMEM
 #pragma unroll 1
                         for (int c = 0; c < 4; ++c) {
-                            uint32_t v[32];
-                            tmem_ld32(tO + c * 32, v);
+                            uint32_t w[32];
+                            tmem_ld32(tO + c * 32, w);
                             tmem_ld_wait();
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-                            tmem_st32(tO + c * 32, v);
+                            for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * alpha);
+                            tmem_st32(tO + c * 32, w);
                         }
                     }
                     l_run *= alpha;
                     m_used = m_new;
                 }
+                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[13], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
-                // pass 2: P = exp2(s*scale - m), bf16, written over S in place (columns 16c..16c+15)
-#pragma unroll 1
+                // P = exp2(s*scale - m) as bf16, written over S in place (32 keys -> 16 columns)
+                float l0 = 0.f, l1 = 0.f;
+#pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_ld_wait();
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
-                        float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-                        float p0 = fast_exp2(fmaf(x0, sl2, -m_use)), p1 = fast_exp2(fmaf(x1, sl2, -m_use));
-                        if (need_mask) {
-                            if (key0 + c * 32 + e >= limit) p0 = 0.f;
-                            if (key0 + c * 32 + e + 1 >= limit) p1 = 0.f;
-                        }
-                        l_run += p0 + p1;
+                        const float p0 = fast_exp2(fmaf(__uint_as_float(v[c][e]), sl2, -m_use));
+                        const float p1 = fast_exp2(fmaf(__uint_as_float(v[c][e + 1]), sl2, -m_use));
+                        l0 += p0; l1 += p1;
                         pk[e >> 1] = pack2<__nv_bfloat16>(p0, p1);
                     }
                     tmem_st16(tS + c * 16, pk);
                 }
+                l_run += l0 + l1;
                 tmem_st_wait();
+                if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
             }
             tc_fence_before();
             mbar_arrive(bar(B_PFULL + t));
@@ -329,8 +356,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
         }
     } else if (warp < MMA_WARP) {
         // =========================== loaders ===========================
-        const int lt = tid - LOADER_WARP0 * 32;        // 0..127
-        const int col = lt & 15, rbase = lt >> 4;      // 16-byte chunk of the row; rows rbase + 8 i
+        const int lt = tid - LOADER_WARP0 * 32;        // 0..63
+        const int col = lt & 15, rbase = lt >> 4;      // 16-byte chunk of the row; rows rbase + 4 i
         const uint32_t half_off = (col >> 3) * REGION;
         const int c8 = col & 7;
         const char* qp = static_cast<const char*>(a.q);
@@ -341,81 +368,67 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
         const int32_t* bt = a.block_tables + (int64_t)seq * a.bt_stride;
         // Q: 256 rows (two tiles), rows >= M zero-filled
 #pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-            const int row = rbase + 8 * i;
+        for (int i = 0; i < 64; ++i) {
+            const int row = rbase + 4 * i;
             const bool okr = row < M;
             const int qi = okr ? row / G : 0, qg = okr ? row % G : 0;
             const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
             const uint32_t dst = sQ + (row >> 7) * (2 * REGION) + half_off + (row & 127) * 128 + ((c8 ^ (row & 7)) << 4);
             cp_async_16(dst, src, okr ? 16 : 0);
         }
-        cp_async_commit();
-        // items: 0 = Q, 1 + 2 jj = K(jj), 2 + 2 jj = V(jj); "full" is signalled two items late so that
-        // up to three groups are in flight per thread
-        auto full_bar = [&](int item) -> uint32_t {
-            if (item == 0) return bar(B_QFULL);
-            const int jj = (item - 1) >> 1;
-            return bar(((item - 1) & 1 ? B_VFULL : B_KFULL) + (jj & 1));
-        };
-        const int items = 1 + 2 * n;
-        bool alive = true;
-        for (int jj = 0; jj < n && alive; ++jj) {
-            const int stage = jj & 1;
-            const uint32_t par_empty = ((jj >> 1) & 1) ^ 1;
-            // row sources of this tile (shared by K and V)
-            int64_t off[16];
-            int kind[16];  // 0 zero-fill, 1 cache, 2 in-flight
+        cp_async_arrive(bar(B_QFULL));
+        // Row-source tables: for every key row of a tile, where its K and V bytes start (nullptr = row
+        // past the end, zero-filled).  Each loader thread resolves two rows (page-table lookup), the
+        // table of the NEXT tile is built while this tile's copies are issued.
+        const char** tabK = reinterpret_cast<const char**>(gbase + OFF_TAB);   // [2][128]
+        const char** tabV = tabK + 2 * TILE_N;                                   // [2][128]
+        auto build_table = [&](int jj) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int p = (t0 + jj) * TILE_N + rbase + 8 * i;
-                kind[i] = 0; off[i] = 0;
+            for (int h = 0; h < 2; ++h) {
+                const int row = lt + 64 * h;
+                const int p = (t0 + jj) * TILE_N + row;
+                const char *pk = nullptr, *pv = nullptr;
                 if (p < ctx) {
                     const int j = p / a.page_size;
                     const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
                     if (pid >= 0 && pid < a.num_pages) {
-                        kind[i] = 1;
-                        off[i] = (pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD + col * 8) << 1;
+                        const int64_t o = (pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1;
+                        pk = kcp + o; pv = vcp + o;
                     }
                 } else if (p < total) {
-                    kind[i] = 2;
-                    off[i] = kv0 + (p - ctx);
+                    const int64_t r = kv0 + (p - ctx);
+                    pk = kp + ((r * a.k_rs + kvh * HD) << 1);
+                    pv = vp + ((r * a.v_rs + kvh * HD) << 1);
                 }
+                tabK[(jj & 1) * TILE_N + row] = pk;
+                tabV[(jj & 1) * TILE_N + row] = pv;
             }
+        };
+        auto loaders_sync = [&]() { asm volatile("bar.sync 1, 64;\n" ::: "memory"); };
+        build_table(0);
+        loaders_sync();
+        bool alive = true;
+        for (int jj = 0; jj < n && alive; ++jj) {
+            const int stage = jj & 1;
+            const uint32_t par_empty = ((jj >> 1) & 1) ^ 1;
+            if (jj + 1 < n) build_table(jj + 1);
 #pragma unroll
             for (int which = 0; which < 2; ++which) {  // 0: K tile, 1: V tile
                 bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 const uint32_t dbase = (which ? sV : sK) + stage * ITEM_BYTES + half_off;
-                const char* cache = which ? vcp : kcp;
-                const char* fresh = which ? vp : kp;
-                const int64_t frs = which ? a.v_rs : a.k_rs;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int row = rbase + 8 * i;
-                    const char* src = qp;
-                    if (kind[i] == 1) src = cache + off[i];
-                    else if (kind[i] == 2) src = fresh + ((off[i] * frs + kvh * HD + col * 8) << 1);
-                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), src, kind[i] ? 16 : 0);
+                const char* const* tab = (which ? tabV : tabK) + stage * TILE_N;
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) {
+                    const int row = rbase + 4 * i;
+                    const char* rp = tab[row];
+                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
                 }
-                cp_async_commit();
-                const int item = 1 + 2 * jj + which;
-                if (item >= 2) {
-                    cp_async_wait<2>();
-                    fence_async_proxy();
-                    mbar_arrive(full_bar(item - 2));
-                }
+                cp_async_arrive(bar((which ? B_VFULL : B_KFULL) + stage));
             }
+            loaders_sync();  // next tile's table is complete; this tile's table may be overwritten after the next sync
         }
-        if (alive) {
-            cp_async_wait<1>();
-            fence_async_proxy();
-            if (items >= 2) mbar_arrive(full_bar(items - 2));
-            cp_async_wait<0>();
-            fence_async_proxy();
-            mbar_arrive(full_bar(items - 1));
-        } else {
-            cp_async_wait<0>();
-        }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
     } else if (lane == 0) {
         // =========================== MMA issuer (one thread) ===========================
         constexpr uint32_t ID_QK = instr_desc(false), ID_PV = instr_desc(true);
@@ -437,6 +450,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
         };
         bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1) && mbar_wait(bar(B_KFULL), 0, abort_flag, 7, 0);
         if (ok) {
+            fence_async_proxy();  // the cp.async writes (generic proxy) must be visible to the tensor pipe's reads
             tc_fence_after();
             issue_qk(0, 0); tc_commit(bar(B_SFULL + 0));
             issue_qk(1, 0); tc_commit(bar(B_SFULL + 1));
@@ -448,11 +462,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
             ok = mbar_wait(bar(B_VFULL + st), (jj >> 1) & 1, abort_flag, 8, jj) &&
                  mbar_wait(bar(B_PFULL + 0), jj & 1, abort_flag, 9, jj);
             if (!ok) break;
+            fence_async_proxy();
             tc_fence_after();
             issue_pv(0, jj);
             if (more) {
                 ok = mbar_wait(bar(B_KFULL + (st ^ 1)), ((jj + 1) >> 1) & 1, abort_flag, 10, jj + 1);
                 if (!ok) break;
+                fence_async_proxy();
                 tc_fence_after();
                 issue_qk(0, jj + 1); tc_commit(bar(B_SFULL + 0));
             }
@@ -469,6 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
         if (ok) tc_commit(bar(B_OFULL));
     }
 
+    if (tid == 0 && prof_thread()) atomicAdd(&g_prof[0], (unsigned long long)(clock64() - cta_c0));
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
@@ -503,6 +520,16 @@ int read_tc5_status(int out[4]) {
     int zero[4] = {0, 0, 0, 0};
     e = cudaMemcpyToSymbol(tc5::g_status, zero, sizeof(zero));
     if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "cudaMemcpyToSymbol(g_status): %s", cudaGetErrorString(e));
+    return DLX_OK;
+}
+
+int tc5_profile(int enable, unsigned long long out[16]) {
+    cudaError_t e = cudaSuccess;
+    if (out != nullptr) e = cudaMemcpyFromSymbol(out, tc5::g_prof, sizeof(unsigned long long) * 16);
+    unsigned long long zero[16] = {};
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof, zero, sizeof(zero));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof_on, &enable, sizeof(int));
+    if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "tc5_profile: %s", cudaGetErrorString(e));
     return DLX_OK;
 }
 

@@ -115,6 +115,10 @@ extern "C" int dlx_debug_device_status(int32_t out[4]) {
     return DLX_OK;
 }
 
+extern "C" int dlx_debug_profile(int enable, uint64_t out[16]) {
+    return tc5_profile(enable, reinterpret_cast<unsigned long long*>(out));
+}
+
 extern "C" int64_t dlx_decode_attn_workspace_bytes(const dlx_decode_attn_params* p) {
     const int rc = validate_decode(p);
     if (rc != DLX_OK) return -(int64_t)rc;

@@ -152,6 +152,15 @@ int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream);
  */
 int dlx_debug_device_status(int32_t out[4]);
 
+/*
+ * Debug aid with no counterpart in the reference: cycle accounting inside the tcgen05 kernel.  While
+ * enabled, CTA (0,0,0) of every launch adds clock64() deltas to a device array: [0] CTA lifetime,
+ * [1..11] cycles spent at each mbarrier wait site, [12..14] softmax pass 1 / accumulator rescale /
+ * pass 2 of Q tile 0.  The call synchronises, copies the array to the HOST array `out` (may be
+ * NULL), clears it, and sets the switch to `enable`.
+ */
+int dlx_debug_profile(int enable, uint64_t out[16]);
+
 #ifdef __cplusplus
 }
 #endif
