@@ -18,6 +18,7 @@ struct DecodeArgs {
     int hq, hkv, group, page_size;
     int mask_mode, dbs;
     int num_splits, m_blocks;
+    int tma_box_rows;  // tcgen05 kernel: rows per TMA box (0 = cached tiles are not fetched by TMA)
     float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -38,6 +39,6 @@ int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st);
 // Copies out and clears the device status word of the tcgen05 kernel (synchronises the device).
 int read_tc5_status(int out[4]);
 // Cycle accounting of CTA (0,0,0) of the tcgen05 kernel: copy out (if out != null), clear, and switch on/off.
-int tc5_profile(int enable, unsigned long long out[16]);
+int tc5_profile(int enable, unsigned long long out[24]);
 
 }  // namespace dlx

@@ -9,11 +9,13 @@
 // Warp roles (352 threads, up to 184 registers each so a softmax thread holds its whole S row):
 //   warps 0-3   softmax warpgroup of Q tile 0: thread <-> TMEM lane <-> query row
 //   warps 4-7   softmax warpgroup of Q tile 1
-//   warps 8-9   loaders: 16-byte cp.async of Q and of K/V tiles (128 keys) into 128B-swizzled
-//               shared memory (the canonical K-major / MN-major UMMA layouts), any page size, the
-//               cached prefix and the in-flight rows as ONE key axis, rows past the end zero-filled;
-//               completion is signalled by cp.async.mbarrier.arrive, so loads run as far ahead as
-//               the two-stage K and V rings allow
+//   warps 8-9   loaders.  K/V tiles (128 keys) that lie wholly inside the cached prefix are fetched by
+//               TMA (cp.async.bulk.tensor, 4-D map {hd, Hkv, page row, page} with 128-byte swizzle, plain
+//               per-CTA loads): one thread issues two boxes per tile and the copy engine keeps far more
+//               bytes in flight than LDGSTS can (16-byte cp.async tops out near 14 B/clk/SM here).
+//               The tile that holds the end of the prefix and the in-flight rows, and every tile when
+//               the page size does not fit a box, go through 16-byte cp.async with the same swizzle:
+//               any page size, prefix and in-flight rows as ONE key axis, rows past the end zero-filled
 //   warp 10     one elected thread issues tcgen05.mma: S_t = Q_t K^T (SS form) into TMEM, and
 //               O_t += P_t V (TS form: P is read from TMEM, V^T from shared memory), and
 //               tcgen05.commit to the mbarriers that hand tiles back and forth
@@ -26,6 +28,14 @@
 // in a device status word, drains, frees TMEM and returns (no trap, the context stays usable).
 //
 // Reference semantics: diffulex_kernel/python/dllm_flash_attn.py:163-347 and :632-637.
+#include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (resolved at run time, no libcuda link)
+
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
 #include "dlx_common.cuh"
 #include "decode_attn.cuh"
 
@@ -42,7 +52,9 @@ constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + STAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 2 stages x 128 rows
-constexpr int SMEM_BYTES = OFF_TAB + 4 * TILE_N * 8 + 1024;  // + slack for 1024-byte alignment
+constexpr int OFF_BT = OFF_TAB + 4 * TILE_N * 8;   // this sequence's page ids
+constexpr int BT_SLOTS = 4096;                     // 16 KiB: 1 M tokens at 256-token pages
+constexpr int SMEM_BYTES = OFF_BT + BT_SLOTS * 4 + 1024;  // + slack for 1024-byte alignment
 constexpr int NUM_THREADS = 352;
 constexpr int LOADER_WARP0 = 8, MMA_WARP = 10;
 constexpr int NUM_LOADERS = 64;
@@ -54,7 +66,7 @@ enum { B_QFULL = 0, B_KFULL = 1, B_VFULL = 3, B_KEMPTY = 5, B_VEMPTY = 7, B_SFUL
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
 // Optional cycle accounting of CTA (0,0,0): [0] CTA lifetime, [role] cycles spent in that wait site,
 // [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
-__device__ unsigned long long g_prof[16];
+__device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
 __device__ __forceinline__ bool prof_thread() {
     return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && ((threadIdx.x & 127) == 0 || threadIdx.x == 320);
@@ -102,10 +114,37 @@ __device__ __forceinline__ void fence_async_proxy() { asm volatile("fence.proxy.
 __device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// One TMA box global -> shared, completion counted in bytes on `bar`.  Coordinates innermost first; c0 (elements of
+// 2 bytes) is 0 or 64, i.e. a multiple of 16 bytes as the copy engine requires.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
+}
+// 2^x for a pair, on the FMA pipe: round-to-nearest split x = n + f (|f| <= 0.5) with the 1.5*2^23 magic
+// constant, 2^f by a degree-3 minimax polynomial (relative error 1.2e-4, below bf16 rounding of P), and n
+// added into the exponent field.  Inputs are clamped at -126 (2^-126 stands in for 0; -inf is a legal input).
+constexpr int POLY_PAIRS_OF_4 = 2;  // of every 4 consecutive pairs, this many use the polynomial, the rest MUFU
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -126.f); x.y = fmaxf(x.y, -126.f);
+    const float2 magic = make_float2(12582912.f, 12582912.f);
+    const float2 r = __fadd2_rn(x, magic);
+    const float2 nf = __fadd2_rn(r, make_float2(-12582912.f, -12582912.f));
+    const float2 f = __ffma2_rn(nf, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(f, make_float2(0.05459282f, 0.05459282f), make_float2(0.24221784f, 0.24221784f));
+    p = __ffma2_rn(p, f, make_float2(0.69336860f, 0.69336860f));
+    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
+    p.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(r.x) << 23));
+    p.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(r.y) << 23));
+    return p;
 }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
@@ -167,7 +206,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
     extern __shared__ unsigned char smem_raw[];
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -268,12 +308,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
                         for (int e = 0; e < 32; ++e)
                             if (key0 + c * 32 + e >= limit) v[c][e] = 0xff800000u;  // -inf
                 }
-                float mx = -INFINITY;
+                float mx4[4];  // four independent chains: the max is latency-, not issue-bound
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 4; ++c) {
+                    mx4[c] = -INFINITY;
 #pragma unroll
                     for (int e = 0; e < 32; e += 2)
-                        mx = max3(mx, __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
+                        mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
+                }
+                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                 if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_new = fmaxf(m_used, mx * sl2);
                 const bool need = (m_new > m_used) && (m_used == -INFINITY || m_new - m_used > 8.f);
@@ -296,20 +339,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
                 if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[13], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
                 // P = exp2(s*scale - m) as bf16, written over S in place (32 keys -> 16 columns)
-                float l0 = 0.f, l1 = 0.f;
+                // Element pairs go through packed f32x2 FMA-pipe ops.  The exponential itself is split
+                // between the MUFU unit (ex2.approx, 4 lanes/clk per SM sub-partition) and a degree-3
+                // polynomial on the FMA pipe, because at 128 x 128 exponentials per tile the MUFU alone
+                // would be as slow as the tensor pipe.
+                float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
+                const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_use, -m_use);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
-                        const float p0 = fast_exp2(fmaf(__uint_as_float(v[c][e]), sl2, -m_use));
-                        const float p1 = fast_exp2(fmaf(__uint_as_float(v[c][e + 1]), sl2, -m_use));
-                        l0 += p0; l1 += p1;
-                        pk[e >> 1] = pack2<__nv_bfloat16>(p0, p1);
+                        float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
+                        float2 p;
+                        if (((e >> 1) & 3) < POLY_PAIRS_OF_4) p = exp2_poly2(x);
+                        else p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                        if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
+                        pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                     }
                     tmem_st16(tS + c * 16, pk);
                 }
-                l_run += l0 + l1;
+                lacc0 = __fadd2_rn(lacc0, lacc1);
+                l_run += lacc0.x + lacc0.y;
                 tmem_st_wait();
                 if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
             }
@@ -365,18 +416,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
         const char* vp = static_cast<const char*>(a.v);
         const char* kcp = static_cast<const char*>(a.k_cache);
         const char* vcp = static_cast<const char*>(a.v_cache);
-        const int32_t* bt = a.block_tables + (int64_t)seq * a.bt_stride;
-        // Q: 256 rows (two tiles), rows >= M zero-filled
+        const int32_t* bt_g = a.block_tables + (int64_t)seq * a.bt_stride;
+        // This sequence's page ids go to shared memory once (a per-tile global lookup would put a DRAM/L2
+        // round trip in front of every tile's copies).  Longer tables than the slot fall back to global.
+        int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT);
+        const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
+        const bool bt_in_smem = pages_needed <= BT_SLOTS;
+        if (bt_in_smem)
+            for (int j = lt; j < pages_needed; j += NUM_LOADERS) bt_s[j] = bt_g[j];
+        const int32_t* bt = bt_in_smem ? bt_s : bt_g;
+        // Q: 256 rows (two tiles), rows >= M zero-filled; row r is token r / G, head r % G, walked incrementally
+        {
+            int qi = rbase / G, qg = rbase % G;
 #pragma unroll 4
-        for (int i = 0; i < 64; ++i) {
-            const int row = rbase + 4 * i;
-            const bool okr = row < M;
-            const int qi = okr ? row / G : 0, qg = okr ? row % G : 0;
-            const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
-            const uint32_t dst = sQ + (row >> 7) * (2 * REGION) + half_off + (row & 127) * 128 + ((c8 ^ (row & 7)) << 4);
-            cp_async_16(dst, src, okr ? 16 : 0);
+            for (int i = 0; i < 64; ++i) {
+                const int row = rbase + 4 * i;
+                const bool okr = row < M;
+                const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
+                const uint32_t dst = sQ + (row >> 7) * (2 * REGION) + half_off + (row & 127) * 128 + ((c8 ^ (row & 7)) << 4);
+                cp_async_16(dst, okr ? src : qp, okr ? 16 : 0);
+                qg += 4;
+                while (qg >= G) { qg -= G; ++qi; }
+            }
         }
         cp_async_arrive(bar(B_QFULL));
+        asm volatile("bar.sync 1, 64;\n" ::: "memory");  // page ids visible to both loader warps
         // Row-source tables: for every key row of a tile, where its K and V bytes start (nullptr = row
         // past the end, zero-filled).  Each loader thread resolves two rows (page-table lookup), the
         // table of the NEXT tile is built while this tile's copies are issued.
@@ -405,26 +469,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
             }
         };
         auto loaders_sync = [&]() { asm volatile("bar.sync 1, 64;\n" ::: "memory"); };
-        build_table(0);
+        if (!(a.tma_box_rows > 0 && (t0 + 1) * TILE_N <= ctx)) build_table(0);
         loaders_sync();
         bool alive = true;
         for (int jj = 0; jj < n && alive; ++jj) {
             const int stage = jj & 1;
             const uint32_t par_empty = ((jj >> 1) & 1) ^ 1;
-            if (jj + 1 < n) build_table(jj + 1);
+            const bool recl = prof_thread();
+            long long cl = recl ? clock64() : 0;
+            // regular tile: all 128 keys are cached rows and the page geometry fits TMA boxes
+            const int p0 = (t0 + jj) * TILE_N;
+            const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
+            const bool next_by_tma = a.tma_box_rows > 0 && p0 + 2 * TILE_N <= ctx;
+            if (jj + 1 < n && !next_by_tma) build_table(jj + 1);
+            if (recl) { const long long c1 = clock64(); atomicAdd(&g_prof[15], (unsigned long long)(c1 - cl)); cl = c1; }
 #pragma unroll
             for (int which = 0; which < 2; ++which) {  // 0: K tile, 1: V tile
                 bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                const uint32_t dbase = (which ? sV : sK) + stage * ITEM_BYTES + half_off;
-                const char* const* tab = (which ? tabV : tabK) + stage * TILE_N;
+                const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
+                if (by_tma) {
+                    if (lt == 0) {
+                        mbar_arrive_expect_tx(full, ITEM_BYTES);
+                        const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
+                        const CUtensorMap* map = which ? &tm_v : &tm_k;
+                        const int rows = a.tma_box_rows;               // min(128, page_size)
+                        for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
+                            const int j = (p0 + r0) / a.page_size;
+                            const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
+                            const int rin = (p0 + r0) - j * a.page_size;
+                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
+                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
+                        }
+                    } else {
+                        mbar_arrive(full);
+                    }
+                } else {
+                    const uint32_t dbase = (which ? sV : sK) + stage * ITEM_BYTES + half_off;
+                    const char* const* tab = (which ? tabV : tabK) + stage * TILE_N;
 #pragma unroll 8
-                for (int i = 0; i < 32; ++i) {
-                    const int row = rbase + 4 * i;
-                    const char* rp = tab[row];
-                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
+                    for (int i = 0; i < 32; ++i) {
+                        const int row = rbase + 4 * i;
+                        const char* rp = tab[row];
+                        cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
+                    }
+                    cp_async_arrive(full);
                 }
-                cp_async_arrive(bar((which ? B_VFULL : B_KFULL) + stage));
+                if (recl) { const long long c1 = clock64(); atomicAdd(&g_prof[18 + which], (unsigned long long)(c1 - cl)); cl = c1; }
             }
             loaders_sync();  // next tile's table is complete; this tile's table may be overwritten after the next sync
         }
@@ -464,13 +555,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
             if (!ok) break;
             fence_async_proxy();
             tc_fence_after();
-            issue_pv(0, jj);
+            { const bool r_ = prof_thread(); const long long c_ = r_ ? clock64() : 0; issue_pv(0, jj); if (r_) atomicAdd(&g_prof[16], (unsigned long long)(clock64() - c_)); }
             if (more) {
                 ok = mbar_wait(bar(B_KFULL + (st ^ 1)), ((jj + 1) >> 1) & 1, abort_flag, 10, jj + 1);
                 if (!ok) break;
                 fence_async_proxy();
                 tc_fence_after();
-                issue_qk(0, jj + 1); tc_commit(bar(B_SFULL + 0));
+                { const bool r_ = prof_thread(); const long long c_ = r_ ? clock64() : 0; issue_qk(0, jj + 1); if (r_) atomicAdd(&g_prof[17], (unsigned long long)(clock64() - c_)); }
+                tc_commit(bar(B_SFULL + 0));
             }
             ok = mbar_wait(bar(B_PFULL + 1), jj & 1, abort_flag, 11, jj);
             if (!ok) break;
@@ -499,7 +591,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) decode_attn_tc5_kernel(const D
 
 bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows > 128 && rows <= 256; }
 
-int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st) {
+// ---- TMA descriptors for the caches -----------------------------------------------------------
+// A 4-D map {head_dim, Hkv, page row, page} of one cache tensor; box {64, 1, rows, 1}, 128-byte swizzle.
+// Encoding is a host-only computation on (pointer, sizes, strides); results are memoised.
+namespace {
+struct MapKey {
+    const void* ptr; int64_t page_stride, token_stride, num_pages; int hkv, page_size, rows;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && page_stride == o.page_stride && token_stride == o.token_stride &&
+               num_pages == o.num_pages && hkv == o.hkv && page_size == o.page_size && rows == o.rows;
+    }
+};
+struct MapEntry { MapKey key; CUtensorMap map; };
+std::mutex g_map_mutex;
+std::vector<MapEntry> g_maps;
+size_t g_map_next = 0;
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                             const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn encode_fn() {
+    static EncodeFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<EncodeFn>(f);
+    }();
+    return fn;
+}
+int cache_map(const MapKey& k, CUtensorMap* out) {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    for (const MapEntry& e : g_maps)
+        if (e.key == k) { *out = e.map; return DLX_OK; }
+    EncodeFn enc = encode_fn();
+    if (enc == nullptr) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from this driver");
+    const cuuint64_t gdim[4] = {(cuuint64_t)tc5::HD, (cuuint64_t)k.hkv, (cuuint64_t)k.page_size, (cuuint64_t)k.num_pages};
+    const cuuint64_t gstr[3] = {(cuuint64_t)tc5::HD * 2, (cuuint64_t)k.token_stride * 2, (cuuint64_t)k.page_stride * 2};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)k.rows, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    MapEntry e;
+    e.key = k;
+    const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k.ptr), gdim, gstr, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
+    if (g_maps.size() < 512) g_maps.push_back(e);
+    else { g_maps[g_map_next] = e; g_map_next = (g_map_next + 1) % g_maps.size(); }
+    *out = e.map;
+    return DLX_OK;
+}
+}  // namespace
+
+int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     static bool attr_done[16] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -509,8 +653,28 @@ int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "cudaFuncSetAttribute(tc5 smem=%d): %s", tc5::SMEM_BYTES, cudaGetErrorString(e));
         attr_done[dev] = true;
     }
+    DecodeArgs a = a_in;
+    CUtensorMap tm_k, tm_v;
+    memset(&tm_k, 0, sizeof(tm_k));
+    memset(&tm_v, 0, sizeof(tm_v));
+    // TMA serves tiles of 128 cached keys when a tile is a whole number of equal boxes: the page size is a
+    // multiple of 128 rows, or divides 128 and is a multiple of the 8-row swizzle period.
+    a.tma_box_rows = 0;
+    const int ps = a.page_size;
+    const bool fits = a.max_blocks > 0 && a.num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
+    const bool strides_ok = a.token_stride * 2 % 16 == 0 && a.page_stride * 2 % 16 == 0 &&
+                            a.page_stride * 2 < (1ll << 40) && a.num_pages < (1ll << 31);
+    if (fits && strides_ok && getenv("DLX_TC5_NO_TMA") == nullptr) {
+        const int rows = ps < 128 ? ps : 128;
+        MapKey kk{a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
+        MapKey kv{a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
+        int rc = cache_map(kk, &tm_k);
+        if (rc == DLX_OK) rc = cache_map(kv, &tm_v);
+        if (rc != DLX_OK) return rc;
+        a.tma_box_rows = rows;
+    }
     dim3 grid(a.num_splits, a.hkv, a.num_seqs), block(tc5::NUM_THREADS);
-    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a);
+    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, tm_k, tm_v);
     return check_launch("decode_attn_tc5_kernel");
 }
 
@@ -523,10 +687,10 @@ int read_tc5_status(int out[4]) {
     return DLX_OK;
 }
 
-int tc5_profile(int enable, unsigned long long out[16]) {
+int tc5_profile(int enable, unsigned long long out[24]) {
     cudaError_t e = cudaSuccess;
-    if (out != nullptr) e = cudaMemcpyFromSymbol(out, tc5::g_prof, sizeof(unsigned long long) * 16);
-    unsigned long long zero[16] = {};
+    if (out != nullptr) e = cudaMemcpyFromSymbol(out, tc5::g_prof, sizeof(unsigned long long) * 24);
+    unsigned long long zero[24] = {};
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof, zero, sizeof(zero));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof_on, &enable, sizeof(int));
     if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "tc5_profile: %s", cudaGetErrorString(e));

@@ -115,7 +115,7 @@ extern "C" int dlx_debug_device_status(int32_t out[4]) {
     return DLX_OK;
 }
 
-extern "C" int dlx_debug_profile(int enable, uint64_t out[16]) {
+extern "C" int dlx_debug_profile(int enable, uint64_t out[24]) {
     return tc5_profile(enable, reinterpret_cast<unsigned long long*>(out));
 }
 

@@ -159,7 +159,7 @@ int dlx_debug_device_status(int32_t out[4]);
  * pass 2 of Q tile 0.  The call synchronises, copies the array to the HOST array `out` (may be
  * NULL), clears it, and sets the switch to `enable`.
  */
-int dlx_debug_profile(int enable, uint64_t out[16]);
+int dlx_debug_profile(int enable, uint64_t out[24]);
 
 #ifdef __cplusplus
 }
