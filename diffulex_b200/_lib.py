@@ -31,7 +31,7 @@ class DecodeAttnParams(ctypes.Structure):
         ("struct_bytes", c_uint32), ("dtype", c_int32),
         ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
         ("out", c_void_p), ("block_tables", c_void_p), ("context_lens", c_void_p), ("cu_seqlens_q", c_void_p),
-        ("cu_seqlens_kv", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_int64),
+        ("cu_seqlens_kv", c_void_p), ("seq_order", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_int64),
         ("q_row_stride", c_int64), ("k_row_stride", c_int64), ("v_row_stride", c_int64), ("out_row_stride", c_int64),
         ("cache_page_stride", c_int64), ("cache_token_stride", c_int64), ("block_table_stride", c_int64),
         ("num_pages", c_int64),

@@ -9,6 +9,7 @@ struct DecodeArgs {
     const void *q, *k, *v, *k_cache, *v_cache;
     void* out;
     const int32_t *block_tables, *context_lens, *cu_q, *cu_kv;  // cu_kv == nullptr: in-flight rows follow cu_q
+    const int32_t* seq_order;  // optional [num_seqs]: sequence handled by grid slot z (longest first balances SMs)
     float* ws_o;    // [num_splits, total_q, Hq, hd] normalised fp32 partial outputs
     float* ws_lse;  // [num_splits, total_q, Hq]     log2-sum-exp of each partial (-inf: nothing seen)
     int64_t q_rs, k_rs, v_rs, o_rs;     // row strides, elements

@@ -55,10 +55,11 @@ __global__ void __launch_bounds__(C::NT, C::MINB) decode_attn_mma_kernel(const D
 
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / a.m_blocks, mb = blockIdx.y % a.m_blocks;
-    const int seq = blockIdx.z;
+    const int seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp % WM, wn = warp / WM;
     const int G = a.group;
+    if (seq < 0 || seq >= a.num_seqs) return;
 
     const int q0 = a.cu_q[seq];
     const int qn = a.cu_q[seq + 1] - q0;

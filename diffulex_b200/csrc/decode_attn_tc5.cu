@@ -61,7 +61,9 @@ constexpr int NUM_LOADERS = 64;
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
 
 // barrier slots (8 bytes each) at OFF_BAR
-enum { B_QFULL = 0, B_KFULL = 1, B_VFULL = 3, B_KEMPTY = 5, B_VEMPTY = 7, B_SFULL = 9, B_PFULL = 11, B_OFULL = 13, B_COUNT = 14 };
+enum { B_QFULL = 0, B_KFULL = 1, B_VFULL = 3, B_KEMPTY = 5, B_VEMPTY = 7, B_SFULL = 9, B_PFULL = 11, B_OFULL = 13,
+       B_TURN = 14,  // [tile]: the exponential phases of the two softmax warpgroups take turns on the MUFU unit
+       B_COUNT = 16 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
 // Optional cycle accounting of CTA (0,0,0): [0] CTA lifetime, [role] cycles spent in that wait site,
@@ -82,9 +84,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n.reg .pred p;\n"
+#if DLX_WAIT_HINT
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        "selp.b32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(DLX_WAIT_HINT) : "memory");
+#else
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
         "selp.b32 %0, 1, 0, p;\n}\n"
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+#endif
     return ok != 0;
 }
 // Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
@@ -97,6 +105,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             return true;
         }
         if ((it & 255u) == 255u && *abort_flag) return false;
+#if DLX_WAIT_SLEEP
+        if (it >= 2) __nanosleep(DLX_WAIT_SLEEP);  // a spinning warp must not eat the issue slots of the softmax warp next to it
+#endif
     }
     *abort_flag = 1;
     if (atomicCAS(&g_status[0], 0, 1) == 0) {
@@ -124,6 +135,26 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
 }
+#ifndef DLX_PACK_BY_ALU
+#define DLX_PACK_BY_ALU 0
+#endif
+#ifndef DLX_WAIT_HINT
+#define DLX_WAIT_HINT 0
+#endif
+#ifndef DLX_WAIT_SLEEP
+#define DLX_WAIT_SLEEP 0
+#endif
+#ifndef DLX_PINGPONG
+#define DLX_PINGPONG 1
+#endif
+#ifndef DLX_EXP_BF16X2
+#define DLX_EXP_BF16X2 0
+#endif
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+    uint32_t y;
+    asm("ex2.approx.ftz.bf16x2 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -132,7 +163,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // 2^x for a pair, on the FMA pipe: round-to-nearest split x = n + f (|f| <= 0.5) with the 1.5*2^23 magic
 // constant, 2^f by a degree-3 minimax polynomial (relative error 1.2e-4, below bf16 rounding of P), and n
 // added into the exponent field.  Inputs are clamped at -126 (2^-126 stands in for 0; -inf is a legal input).
-constexpr int POLY_PAIRS_OF_4 = 2;  // of every 4 consecutive pairs, this many use the polynomial, the rest MUFU
+constexpr int POLY_PAIRS_OF_4 = 0;  // of every 4 consecutive pairs, this many use the polynomial, the rest MUFU
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     x.x = fmaxf(x.x, -126.f); x.y = fmaxf(x.y, -126.f);
     const float2 magic = make_float2(12582912.f, 12582912.f);
@@ -209,11 +240,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
     extern __shared__ unsigned char smem_raw[];
-    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.group;
 
     // ---- CTA-uniform problem setup (before any TMEM / barrier state exists) ----
+    if (seq < 0 || seq >= a.num_seqs) return;
     const int q0 = a.cu_q[seq];
     const int qn = a.cu_q[seq + 1] - q0;
     if (qn <= 0 || q0 < 0 || q0 + qn > a.total_q) return;
@@ -225,6 +257,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     }
     const int total = ctx + nnew;
     const int M = min(qn * G, 256);
+    const int NTILE = M > 128 ? 2 : 1;  // Q tiles in use
     int cta_limit = total, full_until = total;
     if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
         const int i_last = (M - 1) / G;
@@ -260,6 +293,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             mbar_init(bar(B_VEMPTY + s), 1);
             mbar_init(bar(B_SFULL + s), 1);
             mbar_init(bar(B_PFULL + s), 128);
+            mbar_init(bar(B_TURN + s), 128);
         }
         mbar_init(bar(B_OFULL), 1);
         *abort_flag = 0;
@@ -288,8 +322,8 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = ctx + min(nnew, ((r / G) / a.dbs + 1) * a.dbs);
         const float sl2 = a.scale_log2;
         float m_used = -INFINITY, l_run = 0.f;
-        bool alive = true;
-        for (int jj = 0; jj < n; ++jj) {
+        bool alive = t < NTILE;
+        for (int jj = 0; jj < n && alive; ++jj) {
             bool ok = mbar_wait(bar(B_SFULL + t), jj & 1, abort_flag, 1 + t, jj);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
@@ -297,17 +331,26 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 const int key0 = (t0 + jj) * TILE_N;
                 const bool rec = prof_thread();
                 long long c0 = rec ? clock64() : 0;
+                if (key0 + TILE_N > full_until) {
+                    // The tile touches a mask boundary (warp-uniform, one or two tiles per CTA): write -inf over
+                    // the hidden scores in TMEM first.  Kept as a small rolled loop on purpose: the common path
+                    // below is fully unrolled and has to stay inside the instruction cache.
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w[32];
+                        tmem_ld32(tS + c * 32, w);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (key0 + c * 32 + e >= limit) w[e] = 0xff800000u;  // -inf
+                        tmem_st32(tS + c * 32, w);
+                    }
+                    tmem_st_wait();
+                }
                 // the whole S row of this thread: 128 fp32 scores in registers, one TMEM round trip
                 uint32_t v[4][32];
                 tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                 tmem_ld_wait();
-                if (key0 + TILE_N > full_until) {  // tile touches a mask boundary (warp-uniform)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (key0 + c * 32 + e >= limit) v[c][e] = 0xff800000u;  // -inf
-                }
                 float mx4[4];  // four independent chains: the max is latency-, not issue-bound
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -337,6 +380,15 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     m_used = m_new;
                 }
                 if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[13], (unsigned long long)(c1 - c0)); c0 = c1; }
+#if DLX_PINGPONG
+                // Ping-pong: tile 0 and tile 1 alternate on the exponentials, so one warpgroup has the MUFU
+                // unit to itself while the tensor pipe works for the other.  Order: (0,jj) (1,jj) (0,jj+1) ...
+                if (NTILE > 1 && (t == 1 || jj > 0)) {
+                    bool okt = mbar_wait(bar(B_TURN + t), (t == 1 ? jj : jj - 1) & 1, abort_flag, 4, jj);
+                    if (!__all_sync(0xffffffffu, okt)) { alive = false; break; }
+                }
+                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[15], (unsigned long long)(c1 - c0)); c0 = c1; }
+#endif
                 const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
                 // P = exp2(s*scale - m) as bf16, written over S in place (32 keys -> 16 columns)
                 // Element pairs go through packed f32x2 FMA-pipe ops.  The exponential itself is split
@@ -351,19 +403,48 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
                         float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
+#if DLX_EXP_BF16X2
+                        // one MUFU op yields both exponentials, already in the packed bf16 form P is stored in
+                        const uint32_t pb = ex2_bf16x2(pack2<__nv_bfloat16>(x.x, x.y));
+                        const float2 p = make_float2(__uint_as_float(pb << 16), __uint_as_float(pb & 0xffff0000u));
+                        pk[e >> 1] = pb;
+#else
                         float2 p;
                         if (((e >> 1) & 3) < POLY_PAIRS_OF_4) p = exp2_poly2(x);
                         else p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-                        if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
+#if DLX_PACK_BY_ALU
+                        // fp32 -> bf16 by integer ops (add half an ulp, keep the high halves, one byte-permute per
+                        // pair): the cvt instruction shares the MUFU pipe with ex2 and would take a third of it.
+                        // The row sum is taken over the rounded values, i.e. over exactly what P V multiplies.
+                        const uint32_t r0 = __float_as_uint(p.x) + 0x8000u, r1 = __float_as_uint(p.y) + 0x8000u;
+                        pk[e >> 1] = __byte_perm(r0, r1, 0x7632);
+                        p = make_float2(__uint_as_float(r0 & 0xffff0000u), __uint_as_float(r1 & 0xffff0000u));
+#else
                         pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+#endif
+#endif
+                        if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
                     }
                     tmem_st16(tS + c * 16, pk);
                 }
                 lacc0 = __fadd2_rn(lacc0, lacc1);
                 l_run += lacc0.x + lacc0.y;
+#if DLX_PINGPONG
+                if (NTILE > 1) mbar_arrive(bar(B_TURN + (t ^ 1)));
+#endif
+                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[14], (unsigned long long)(c1 - c0)); c0 = c1; }
                 tmem_st_wait();
-                if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
+                if (rec) atomicAdd(&g_prof[20], (unsigned long long)(clock64() - c0));
             }
+#if DLX_PINGPONG
+            else if (NTILE > 1) {  // a warp without valid rows only passes the turn on
+                if (t == 1 || jj > 0) {
+                    bool okt = mbar_wait(bar(B_TURN + t), (t == 1 ? jj : jj - 1) & 1, abort_flag, 4, jj);
+                    if (!__all_sync(0xffffffffu, okt)) { alive = false; break; }
+                }
+                mbar_arrive(bar(B_TURN + (t ^ 1)));
+            }
+#endif
             tc_fence_before();
             mbar_arrive(bar(B_PFULL + t));
         }
@@ -372,7 +453,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 3 + t, n);
             alive = __all_sync(0xffffffffu, ok);
         }
-        if (alive && warp_valid) {
+        if (alive && warp_valid && t < NTILE) {
             tc_fence_after();
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
             const int64_t tok = q0 + (row_valid ? r / G : 0);
@@ -434,7 +515,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 const bool okr = row < M;
                 const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
                 const uint32_t dst = sQ + (row >> 7) * (2 * REGION) + half_off + (row & 127) * 128 + ((c8 ^ (row & 7)) << 4);
-                cp_async_16(dst, okr ? src : qp, okr ? 16 : 0);
+                if (row < NTILE * 128) cp_async_16(dst, okr ? src : qp, okr ? 16 : 0);
                 qg += 4;
                 while (qg >= G) { qg -= G; ++qi; }
             }
@@ -544,7 +625,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             fence_async_proxy();  // the cp.async writes (generic proxy) must be visible to the tensor pipe's reads
             tc_fence_after();
             issue_qk(0, 0); tc_commit(bar(B_SFULL + 0));
-            issue_qk(1, 0); tc_commit(bar(B_SFULL + 1));
+            if (NTILE > 1) { issue_qk(1, 0); tc_commit(bar(B_SFULL + 1)); }
             tc_commit(bar(B_KEMPTY + 0));
         }
         for (int jj = 0; jj < n && ok; ++jj) {
@@ -564,13 +645,15 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 { const bool r_ = prof_thread(); const long long c_ = r_ ? clock64() : 0; issue_qk(0, jj + 1); if (r_) atomicAdd(&g_prof[17], (unsigned long long)(clock64() - c_)); }
                 tc_commit(bar(B_SFULL + 0));
             }
-            ok = mbar_wait(bar(B_PFULL + 1), jj & 1, abort_flag, 11, jj);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(1, jj);
+            if (NTILE > 1) {
+                ok = mbar_wait(bar(B_PFULL + 1), jj & 1, abort_flag, 11, jj);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(1, jj);
+            }
             tc_commit(bar(B_VEMPTY + st));
             if (more) {
-                issue_qk(1, jj + 1); tc_commit(bar(B_SFULL + 1));
+                if (NTILE > 1) { issue_qk(1, jj + 1); tc_commit(bar(B_SFULL + 1)); }
                 tc_commit(bar(B_KEMPTY + (st ^ 1)));
             }
         }
@@ -589,7 +672,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
 
 }  // namespace tc5
 
-bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows > 128 && rows <= 256; }
+bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows >= 1 && rows <= 256; }
 
 // ---- TMA descriptors for the caches -----------------------------------------------------------
 // A 4-D map {head_dim, Hkv, page row, page} of one cache tensor; box {64, 1, rows, 1}, 128-byte swizzle.

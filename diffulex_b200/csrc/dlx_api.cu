@@ -44,7 +44,7 @@ static int validate_decode(const dlx_decode_attn_params* p) {
     if (p->kernel < 0 || p->kernel > 2) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: kernel %d", p->kernel);
     if (p->kernel == 2 && !tc5_eligible((int)((int64_t)(p->num_q_heads / p->num_kv_heads) * p->max_q_len > 1 << 20
                                                   ? 1 << 20 : (p->num_q_heads / p->num_kv_heads) * p->max_q_len), p->head_dim))
-        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernel serves head_dim 128 with 129..256 packed rows");
+        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernel serves head_dim 128 with up to 256 packed rows");
     if (p->num_seqs > 65535) return fail(DLX_ERR_UNSUPPORTED, "decode: more than 65535 sequences per call");
     return DLX_OK;
 }
@@ -56,7 +56,7 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     d.mma = plan_mma((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
     d.use_tc5 = p->kernel != 1 && tc5_eligible((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
     if (d.use_tc5) {  // one CTA per (sequence, KV head, split): 256 packed rows, 128-key tiles, 1 CTA/SM
-        d.mma.block_m = 256; d.mma.block_n = 128; d.mma.m_blocks = 1; d.mma.ctas_per_sm = 1;
+        d.mma.block_m = 256; d.mma.block_n = 64; d.mma.m_blocks = 1; d.mma.ctas_per_sm = 1;
     }
     const int64_t max_len = p->max_kv_len > 0 ? p->max_kv_len : (int64_t)p->max_blocks * p->page_size + p->max_q_len;
     const int64_t max_tiles = (max_len + d.mma.block_n - 1) / d.mma.block_n;
@@ -157,7 +157,7 @@ extern "C" int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream) {
     DecodeArgs a{};
     a.q = p->q; a.k = p->k; a.v = p->v; a.k_cache = p->k_cache; a.v_cache = p->v_cache; a.out = p->out;
     a.block_tables = p->block_tables; a.context_lens = p->context_lens;
-    a.cu_q = p->cu_seqlens_q; a.cu_kv = p->cu_seqlens_kv;
+    a.cu_q = p->cu_seqlens_q; a.cu_kv = p->cu_seqlens_kv; a.seq_order = p->seq_order;
     a.q_rs = p->q_row_stride; a.k_rs = p->k_row_stride; a.v_rs = p->v_row_stride; a.o_rs = p->out_row_stride;
     a.page_stride = p->cache_page_stride; a.token_stride = p->cache_token_stride;
     a.bt_stride = p->block_table_stride; a.num_pages = p->num_pages;

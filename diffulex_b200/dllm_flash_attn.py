@@ -27,6 +27,8 @@ import torch
 from . import ops
 from ._lib import DLX_MASK_BLOCK_CAUSAL, DLX_MASK_FULL
 
+_SM_COUNT = 148  # B200
+
 _MASKS = {None: DLX_MASK_FULL, "bd_full": DLX_MASK_FULL, "varlen_full": DLX_MASK_FULL,
           "d2f_block_causal": DLX_MASK_BLOCK_CAUSAL}
 
@@ -52,7 +54,28 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     cu_kv = md.cu_seqlens_k if mode == "static" else None
     num_splits = int(getattr(md, "num_splits", 0) or os.environ.get("DLX_NUM_SPLITS", 0))
     return ops.decode_attn(q, k, v, k_cache, v_cache, md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv,
-                           float(scale), max_q, max_kv, _MASKS[mask_name], dbs, num_splits)
+                           float(scale), max_q, max_kv, _MASKS[mask_name], dbs, num_splits, _longest_first(md, k))
+
+
+def _longest_first(md, k) -> "torch.Tensor | None":
+    """Sequence order for the kernel's grid: longest context first, so that the in-order CTA dispatch
+    behaves like a longest-processing-time schedule when there are more (sequence, KV head) pairs than
+    SMs.  One device-side argsort per metadata state (no host sync), memoised on the metadata object:
+    all layers of a step share it.  The memo is keyed on the context_lens tensor and its version."""
+    ctx = md.context_lens
+    n = int(ctx.numel())
+    if n * int(k.shape[1]) <= _SM_COUNT or os.environ.get("DLX_NO_SEQ_ORDER"):
+        return None
+    key = (ctx.data_ptr(), ctx._version, n)
+    memo = getattr(md, "_dlx_seq_order", None)
+    if memo is not None and memo[0] == key:
+        return memo[1]
+    order = torch.argsort(ctx, descending=True, stable=True).to(torch.int32)
+    try:
+        md._dlx_seq_order = (key, order)
+    except AttributeError:
+        pass
+    return order
 
 
 def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,

@@ -90,7 +90,8 @@ def _(k_cache, v_cache, block_tables, context_lens, seq_lens, cu_seqlens_q, cu_s
 
 # ---- decode attention --------------------------------------------------------------------------
 def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
-                   scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits) -> DecodeAttnParams:
+                   scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits,
+                   seq_order=None) -> DecodeAttnParams:
     if q.dtype not in _DTYPES:
         raise ValueError(f"decode attention is built for bf16, got {q.dtype}")
     total_q, hq, hd = q.shape
@@ -119,6 +120,7 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
     p.context_lens = context_lens.data_ptr()
     p.cu_seqlens_q = cu_seqlens_q.data_ptr()
     p.cu_seqlens_kv = cu_seqlens_kv.data_ptr() if cu_seqlens_kv is not None else None
+    p.seq_order = seq_order.data_ptr() if seq_order is not None else None
     p.total_q, p.num_seqs = total_q, cu_seqlens_q.numel() - 1
     p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
     p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
@@ -132,17 +134,20 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
 def decode_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
                 cu_seqlens_kv: Optional[torch.Tensor], scale: float, max_q_len: int, max_kv_len: int,
-                mask_mode: int, diffusion_block_size: int, num_splits: int) -> torch.Tensor:
-    _need_cuda(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv)
+                mask_mode: int, diffusion_block_size: int, num_splits: int,
+                seq_order: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need_cuda(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, seq_order)
+    if seq_order is not None and (seq_order.numel() != cu_seqlens_q.numel() - 1 or not seq_order.is_contiguous()):
+        raise ValueError("seq_order must be a contiguous int32 permutation of the sequences")
     for name, t in (("block_tables", block_tables), ("context_lens", context_lens), ("cu_seqlens_q", cu_seqlens_q),
-                    ("cu_seqlens_kv", cu_seqlens_kv)):
+                    ("cu_seqlens_kv", cu_seqlens_kv), ("seq_order", seq_order)):
         if t is not None and t.dtype != torch.int32:
             raise ValueError(f"{name} must be int32")
     if block_tables.dim() != 2 or block_tables.stride(1) != 1:
         raise ValueError("block_tables must be [num_seqs, max_blocks] with contiguous rows")
     out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), device=q.device, dtype=q.dtype)
     p = _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
-                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
+                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, seq_order)
     handle = _lib.lib()
     ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
     if ws_bytes < 0:
@@ -157,7 +162,7 @@ def decode_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torc
 
 @decode_attn.register_fake
 def _(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale, max_q_len,
-      max_kv_len, mask_mode, diffusion_block_size, num_splits):
+      max_kv_len, mask_mode, diffusion_block_size, num_splits, seq_order=None):
     return q.new_empty(q.shape)
 
 

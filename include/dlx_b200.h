@@ -117,6 +117,9 @@ typedef struct dlx_decode_attn_params {
     const int32_t* context_lens; /* [num_seqs]                                                         */
     const int32_t* cu_seqlens_q; /* [num_seqs + 1]                                                     */
     const int32_t* cu_seqlens_kv;/* [num_seqs + 1] in-flight offsets, or NULL (= cu_seqlens_q)         */
+    const int32_t* seq_order;    /* optional [num_seqs] permutation: sequence taken by the i-th group of
+                                    CTAs.  Longest context first lets the hardware's in-order CTA dispatch
+                                    act as a longest-processing-time schedule.  NULL = identity          */
     void* workspace;             /* split-K scratch, >= dlx_decode_attn_workspace_bytes(); may be NULL
                                     when that returns 0                                                */
     int64_t workspace_bytes;

@@ -113,7 +113,7 @@ def test_load_bit_exact(name, dlx, golden_dir):
 @pytest.mark.parametrize("num_splits", [0, 1, 3])
 @pytest.mark.parametrize("kernel", ["auto", "mma"])
 def test_attention_matches_golden_and_oracle(name, mode, num_splits, kernel, dlx, golden_dir, monkeypatch):
-    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128, 129..256 packed rows)
+    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128, up to 256 packed rows)
     # and the mma.sync kernel elsewhere; "mma" forces the mma.sync kernel everywhere
     monkeypatch.setenv("DLX_DECODE_KERNEL", {"auto": "0", "mma": "1"}[kernel])
     meta = json.loads((golden_dir / "attn_golden.json").read_text())[name]
@@ -283,8 +283,9 @@ def test_cfg5_attention_properties(dlx, cfg5_problem):
 
 
 def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
-    """Forcing the tcgen05 kernel works on an eligible shape (224 packed rows), is refused on an
-    ineligible one, and the kernel's bounded waits never ran out during this test session."""
+    """Forcing the tcgen05 kernel works on eligible shapes (head_dim 128, up to 256 packed rows: 224 and
+    16 here), is refused on an ineligible one (head_dim 64), and the kernel's bounded waits never ran
+    out during this test session."""
     import ctypes
     from diffulex_b200 import _lib
     monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
@@ -292,8 +293,10 @@ def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
     for splits in (0, 2):
         o = run_decode(dlx, to_dev(p), "static", splits)
         torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)
+    p4 = attn_problem(ATTN_CASES["q4_gqa4"])
+    torch.testing.assert_close(run_decode(dlx, to_dev(p4)).float().cpu(), oracle_out(p4), atol=ATOL, rtol=RTOL)
     with pytest.raises(_lib.DlxError):
-        run_decode(dlx, to_dev(attn_problem(ATTN_CASES["q4_gqa4"])))
+        run_decode(dlx, to_dev(attn_problem(ATTN_CASES["ref_head_dim_64"])))
     st = (ctypes.c_int32 * 4)()
     assert _lib.lib().dlx_debug_device_status(st) == 0
     assert list(st) == [0, 0, 0, 0], f"a bounded wait expired: {list(st)}"
