@@ -15,8 +15,8 @@ One JSON line on rank 0.  ``value`` is the attention's algorithmic KV-read rate,
   barriers; inputs are resident in HBM;
 * ``e2e``: the same step through the Python entry points with HOST inputs: q/k/v and all
   metadata copied from pinned memory, outputs copied back, every step, inside the timed region;
-* ``roofline``: the decode kernel alone, every launch bracketed by CUDA events on its stream
-  (eager launches, same caches), against the measured HBM copy bandwidth;
+* ``roofline``: the decode kernel alone (a graph of the L decode launches, CUDA events around each
+  replay, divided by L), against the measured HBM copy bandwidth;
 * ``cpu_baseline`` / ``--impl reference``: the PyTorch fp32 CPU restatement of the reference's
   attention check (oracle/attn_oracle.py) on the host cores, on a bounded sample (one layer).
 
@@ -247,20 +247,29 @@ def main():
     value = total_kv_bytes / (ms_total * 1e-3) / 1e9
     per_rank_ms = dp.gather_timings(ms_local, dev)
 
-    # ---- roofline: the decode kernel alone, per-launch CUDA events (eager) ----
+    # ---- roofline: the decode kernel alone ----
+    # A second CUDA graph holds only the L decode launches (no store); each replay is bracketed by CUDA
+    # events on the launching stream, so the average launch duration is (replay time / L) with no host
+    # launch gaps inside.  Same caches as above: every launch reads its own layer's 163 MB (cfg2).
     peak, peak_kind = peaks()
-    evs = []
-    for it in range(3 + min(args.steps, 10)):
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
         for p in layers:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
-            a.record()
             dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
-            b.record()
-            if it >= 3:
-                evs.append((a, b))
+    torch.cuda.current_stream().wait_stream(side)
+    g_dec = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_dec):
+        for p in layers:
+            dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+    for _ in range(3):
+        g_dec.replay()
+    evs = []
+    for it in range(min(max(args.steps, 5), 20)):
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(); g_dec.replay(); eb.record()
+        evs.append((ea, eb))
     torch.cuda.synchronize()
-    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    launch_ms = [ea.elapsed_time(eb) / L for ea, eb in evs]
     avg_launch_ms = sum(launch_ms) / len(launch_ms)
     achieved = kv_bytes_layer / (avg_launch_ms * 1e-3) / 1e9
     traffic = NCU_TRAFFIC_BYTES.get(args.workload)

@@ -43,27 +43,36 @@ namespace dlx {
 namespace tc5 {
 
 constexpr int HD = 128;
+constexpr int TILE_M = 128;               // packed query rows per CTA (TMEM lanes)
 constexpr int TILE_N = 128;               // keys per K/V tile
 constexpr int REGION = 128 * 128;         // [128 rows][64 bf16] 128B-swizzled block: 16 KiB
-constexpr int Q_BYTES = 4 * REGION;       // 2 Q tiles x 2 head_dim halves
+constexpr int Q_BYTES = 2 * REGION;       // one Q tile, 2 head_dim halves
 constexpr int ITEM_BYTES = 2 * REGION;    // one K tile or one V tile
-constexpr int STAGES = 2;
+constexpr int KSTAGES = 3, VSTAGES = 2;   // Q K^T runs two tiles ahead of P V, so K needs one stage more
 constexpr int OFF_K = Q_BYTES;
-constexpr int OFF_V = OFF_K + STAGES * ITEM_BYTES;
-constexpr int OFF_BAR = OFF_V + STAGES * ITEM_BYTES;
-constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 2 stages x 128 rows
-constexpr int OFF_BT = OFF_TAB + 4 * TILE_N * 8;   // this sequence's page ids
-constexpr int BT_SLOTS = 4096;                     // 16 KiB: 1 M tokens at 256-token pages
+constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
+constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
+constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 4 slots x 128 rows
+constexpr int OFF_BT = OFF_TAB + 2 * 4 * TILE_N * 8;  // this sequence's page ids
+constexpr int BT_SLOTS = 3072;                     // 12 KiB: 786 k tokens at 256-token pages
 constexpr int SMEM_BYTES = OFF_BT + BT_SLOTS * 4 + 1024;  // + slack for 1024-byte alignment
-constexpr int NUM_THREADS = 352;
-constexpr int LOADER_WARP0 = 8, MMA_WARP = 10;
+constexpr int NUM_THREADS = 224;
+constexpr int LOADER_WARP0 = 4, MMA_WARP = 6;
 constexpr int NUM_LOADERS = 64;
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
+// TMEM columns (512): two S buffers of 128 fp32 columns, two P buffers of 64 columns (128 bf16 keys), O
+constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
 
 // barrier slots (8 bytes each) at OFF_BAR
-enum { B_QFULL = 0, B_KFULL = 1, B_VFULL = 3, B_KEMPTY = 5, B_VEMPTY = 7, B_SFULL = 9, B_PFULL = 11, B_OFULL = 13,
-       B_TURN = 14,  // [tile]: the exponential phases of the two softmax warpgroups take turns on the MUFU unit
-       B_COUNT = 16 };
+enum {
+    B_QFULL = 0, B_KFULL = 1, B_VFULL = 4, B_KEMPTY = 6, B_VEMPTY = 9,
+    B_SFULL = 11,   // [S buffer]
+    B_PFULL = 13,   // [P buffer]: the softmax may be two tiles ahead of the P V that consumes its output and an
+                    // mbarrier can only be one phase ahead of its waiter, hence one barrier per buffer
+    B_OFULL = 15,
+    B_PVDONE = 16,  // the latest P V has run (only waited for before a rescale of O)
+    B_COUNT = 17
+};
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
 // Optional cycle accounting of CTA (0,0,0): [0] CTA lifetime, [role] cycles spent in that wait site,
@@ -71,7 +80,7 @@ __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] 
 __device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
 __device__ __forceinline__ bool prof_thread() {
-    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && ((threadIdx.x & 127) == 0 || threadIdx.x == 320);
+    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && (threadIdx.x == 0 || threadIdx.x == LOADER_WARP0 * 32 || threadIdx.x == MMA_WARP * 32);
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -240,7 +249,9 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
     extern __shared__ unsigned char smem_raw[];
-    const int split = blockIdx.x, kvh = blockIdx.y, seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / a.m_blocks, mb = blockIdx.y % a.m_blocks;
+    const int seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.group;
 
@@ -256,13 +267,15 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         nnew = max(a.cu_kv[seq + 1] - kv0, 0);
     }
     const int total = ctx + nnew;
-    const int M = min(qn * G, 256);
-    const int NTILE = M > 128 ? 2 : 1;  // Q tiles in use
+    const int M = qn * G;               // packed rows of this (sequence, KV head)
+    const int row0 = mb * TILE_M;       // this CTA's rows: row0 .. row0 + 127
+    if (row0 >= M) return;
+    const int rows_here = min(M - row0, TILE_M);
     int cta_limit = total, full_until = total;
     if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
-        const int i_last = (M - 1) / G;
+        const int i_first = row0 / G, i_last = (row0 + rows_here - 1) / G;
         cta_limit = ctx + min(nnew, (i_last / a.dbs + 1) * a.dbs);
-        full_until = ctx + min(nnew, a.dbs);
+        full_until = ctx + min(nnew, (i_first / a.dbs + 1) * a.dbs);
     }
     const int n_tiles = (cta_limit + TILE_N - 1) / TILE_N;
     const int tiles_per_split = (n_tiles + a.num_splits - 1) / a.num_splits;
@@ -271,8 +284,10 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     const int64_t head0 = (int64_t)kvh * G;
     if (t0 >= t1) {
         if (a.num_splits > 1)
-            for (int r = tid; r < M; r += NUM_THREADS)
-                a.ws_lse[((int64_t)split * a.total_q + q0 + r / G) * a.hq + head0 + r % G] = -INFINITY;
+            for (int r = tid; r < rows_here; r += NUM_THREADS) {
+                const int rr = row0 + r;
+                a.ws_lse[((int64_t)split * a.total_q + q0 + rr / G) * a.hq + head0 + rr % G] = -INFINITY;
+            }
         return;
     }
     const int n = t1 - t0;
@@ -286,16 +301,11 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
 
     if (tid == 0) {
         mbar_init(bar(B_QFULL), NUM_LOADERS);
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(B_KFULL + s), NUM_LOADERS);
-            mbar_init(bar(B_VFULL + s), NUM_LOADERS);
-            mbar_init(bar(B_KEMPTY + s), 1);
-            mbar_init(bar(B_VEMPTY + s), 1);
-            mbar_init(bar(B_SFULL + s), 1);
-            mbar_init(bar(B_PFULL + s), 128);
-            mbar_init(bar(B_TURN + s), 128);
-        }
+        for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), NUM_LOADERS); mbar_init(bar(B_KEMPTY + s), 1); }
+        for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128); }
         mbar_init(bar(B_OFULL), 1);
+        mbar_init(bar(B_PVDONE), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -309,32 +319,33 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     const uint32_t tmem = *tmem_slot;
     const long long cta_c0 = (tid == 0 && prof_thread()) ? clock64() : 0;
 
-    if (warp < 8) {
-        // =========================== softmax warpgroups ===========================
-        const int t = warp >> 2;                       // Q tile
-        const int L = tid & 127;                       // TMEM lane == row inside the tile
-        const int r = t * 128 + L;                     // packed row: token r / G, head r % G
-        const bool warp_valid = (t * 128 + (warp & 3) * 32) < M;   // any valid row in this warp?
-        const bool row_valid = r < M;
-        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const uint32_t tS = lane_base + t * 128, tO = lane_base + 256 + t * 128;
+    if (warp < 4) {
+        // =========================== softmax warpgroup ===========================
+        const int L = tid;                             // TMEM lane == row inside the tile
+        const int r = row0 + L;                        // packed row: token r / G, head r % G
+        const bool warp_valid = warp * 32 < rows_here; // any valid row in this warp?
+        const bool row_valid = L < rows_here;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t tO = lane_base + TM_O;
         int limit = total;
         if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = ctx + min(nnew, ((r / G) / a.dbs + 1) * a.dbs);
         const float sl2 = a.scale_log2;
         float m_used = -INFINITY, l_run = 0.f;
-        bool alive = t < NTILE;
+        bool alive = true;
         for (int jj = 0; jj < n && alive; ++jj) {
-            bool ok = mbar_wait(bar(B_SFULL + t), jj & 1, abort_flag, 1 + t, jj);
+            const int b = jj & 1;
+            bool ok = mbar_wait(bar(B_SFULL + b), (jj >> 1) & 1, abort_flag, 1, jj);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
             if (warp_valid) {
+                const uint32_t tS = lane_base + TM_S + b * 128, tP = lane_base + TM_P + b * 64;
                 const int key0 = (t0 + jj) * TILE_N;
                 const bool rec = prof_thread();
                 long long c0 = rec ? clock64() : 0;
                 if (key0 + TILE_N > full_until) {
                     // The tile touches a mask boundary (warp-uniform, one or two tiles per CTA): write -inf over
-                    // the hidden scores in TMEM first.  Kept as a small rolled loop on purpose: the common path
-                    // below is fully unrolled and has to stay inside the instruction cache.
+                    // the hidden scores in TMEM first.  A small rolled loop on purpose: the common path below is
+                    // fully unrolled and should stay inside the instruction cache.
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         uint32_t w[32];
@@ -360,12 +371,17 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                         mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
                 }
                 const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_new = fmaxf(m_used, mx * sl2);
                 const bool need = (m_new > m_used) && (m_used == -INFINITY || m_new - m_used > 8.f);
                 if (__any_sync(0xffffffffu, need)) {
                     const float alpha = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
-                    if (jj > 0) {  // O_t holds the sum over earlier tiles: rescale it in TMEM
+                    if (jj > 0) {
+                        // O holds the sum over earlier tiles: rescale it in TMEM.  P V of the previous tile may
+                        // still be running (S of THIS tile being complete only orders P V up to tile jj - 2,
+                        // because Q K^T runs two tiles ahead), so wait for it explicitly.
+                        bool ok2 = mbar_wait(bar(B_PVDONE), (jj - 1) & 1, abort_flag, 3, jj);
+                        if (!__all_sync(0xffffffffu, ok2)) { alive = false; break; }
+                        tc_fence_after();
 #pragma unroll 1
                         for (int c = 0; c < 4; ++c) {
                             uint32_t w[32];
@@ -379,22 +395,9 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     l_run *= alpha;
                     m_used = m_new;
                 }
-                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[13], (unsigned long long)(c1 - c0)); c0 = c1; }
-#if DLX_PINGPONG
-                // Ping-pong: tile 0 and tile 1 alternate on the exponentials, so one warpgroup has the MUFU
-                // unit to itself while the tensor pipe works for the other.  Order: (0,jj) (1,jj) (0,jj+1) ...
-                if (NTILE > 1 && (t == 1 || jj > 0)) {
-                    bool okt = mbar_wait(bar(B_TURN + t), (t == 1 ? jj : jj - 1) & 1, abort_flag, 4, jj);
-                    if (!__all_sync(0xffffffffu, okt)) { alive = false; break; }
-                }
-                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[15], (unsigned long long)(c1 - c0)); c0 = c1; }
-#endif
+                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
                 const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
-                // P = exp2(s*scale - m) as bf16, written over S in place (32 keys -> 16 columns)
-                // Element pairs go through packed f32x2 FMA-pipe ops.  The exponential itself is split
-                // between the MUFU unit (ex2.approx, 4 lanes/clk per SM sub-partition) and a degree-3
-                // polynomial on the FMA pipe, because at 128 x 128 exponentials per tile the MUFU alone
-                // would be as slow as the tensor pipe.
+                // P = exp2(s*scale - m) as bf16 into this tile's P buffer (32 keys -> 16 columns)
                 float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                 const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_use, -m_use);
 #pragma unroll
@@ -402,58 +405,27 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
-                        float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
-#if DLX_EXP_BF16X2
-                        // one MUFU op yields both exponentials, already in the packed bf16 form P is stored in
-                        const uint32_t pb = ex2_bf16x2(pack2<__nv_bfloat16>(x.x, x.y));
-                        const float2 p = make_float2(__uint_as_float(pb << 16), __uint_as_float(pb & 0xffff0000u));
-                        pk[e >> 1] = pb;
-#else
-                        float2 p;
-                        if (((e >> 1) & 3) < POLY_PAIRS_OF_4) p = exp2_poly2(x);
-                        else p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-#if DLX_PACK_BY_ALU
-                        // fp32 -> bf16 by integer ops (add half an ulp, keep the high halves, one byte-permute per
-                        // pair): the cvt instruction shares the MUFU pipe with ex2 and would take a third of it.
-                        // The row sum is taken over the rounded values, i.e. over exactly what P V multiplies.
-                        const uint32_t r0 = __float_as_uint(p.x) + 0x8000u, r1 = __float_as_uint(p.y) + 0x8000u;
-                        pk[e >> 1] = __byte_perm(r0, r1, 0x7632);
-                        p = make_float2(__uint_as_float(r0 & 0xffff0000u), __uint_as_float(r1 & 0xffff0000u));
-#else
-                        pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
-#endif
-#endif
+                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
+                        const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                         if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
+                        pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                     }
-                    tmem_st16(tS + c * 16, pk);
+                    tmem_st16(tP + c * 16, pk);
                 }
                 lacc0 = __fadd2_rn(lacc0, lacc1);
                 l_run += lacc0.x + lacc0.y;
-#if DLX_PINGPONG
-                if (NTILE > 1) mbar_arrive(bar(B_TURN + (t ^ 1)));
-#endif
-                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[14], (unsigned long long)(c1 - c0)); c0 = c1; }
                 tmem_st_wait();
-                if (rec) atomicAdd(&g_prof[20], (unsigned long long)(clock64() - c0));
+                if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
             }
-#if DLX_PINGPONG
-            else if (NTILE > 1) {  // a warp without valid rows only passes the turn on
-                if (t == 1 || jj > 0) {
-                    bool okt = mbar_wait(bar(B_TURN + t), (t == 1 ? jj : jj - 1) & 1, abort_flag, 4, jj);
-                    if (!__all_sync(0xffffffffu, okt)) { alive = false; break; }
-                }
-                mbar_arrive(bar(B_TURN + (t ^ 1)));
-            }
-#endif
             tc_fence_before();
-            mbar_arrive(bar(B_PFULL + t));
+            mbar_arrive(bar(B_PFULL + b));
         }
-        // ---- epilogue: O_t / l -> global ----
+        // ---- epilogue: O / l -> global ----
         if (alive) {
-            bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 3 + t, n);
+            bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 2, n);
             alive = __all_sync(0xffffffffu, ok);
         }
-        if (alive && warp_valid && t < NTILE) {
+        if (alive && warp_valid) {
             tc_fence_after();
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
             const int64_t tok = q0 + (row_valid ? r / G : 0);
@@ -498,7 +470,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         const char* kcp = static_cast<const char*>(a.k_cache);
         const char* vcp = static_cast<const char*>(a.v_cache);
         const int32_t* bt_g = a.block_tables + (int64_t)seq * a.bt_stride;
-        // This sequence's page ids go to shared memory once (a per-tile global lookup would put a DRAM/L2
+        // This sequence's page ids go to shared memory once (a per-tile global lookup would put an L2
         // round trip in front of every tile's copies).  Longer tables than the slot fall back to global.
         int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT);
         const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
@@ -506,31 +478,29 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         if (bt_in_smem)
             for (int j = lt; j < pages_needed; j += NUM_LOADERS) bt_s[j] = bt_g[j];
         const int32_t* bt = bt_in_smem ? bt_s : bt_g;
-        // Q: 256 rows (two tiles), rows >= M zero-filled; row r is token r / G, head r % G, walked incrementally
+        // Q: this CTA's 128 rows, rows past the end zero-filled; row r is token r / G, head r % G, walked incrementally
         {
-            int qi = rbase / G, qg = rbase % G;
+            int qi = (row0 + rbase) / G, qg = (row0 + rbase) % G;
 #pragma unroll 4
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
                 const int row = rbase + 4 * i;
-                const bool okr = row < M;
+                const bool okr = row < rows_here;
                 const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
-                const uint32_t dst = sQ + (row >> 7) * (2 * REGION) + half_off + (row & 127) * 128 + ((c8 ^ (row & 7)) << 4);
-                if (row < NTILE * 128) cp_async_16(dst, okr ? src : qp, okr ? 16 : 0);
+                cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
                 qg += 4;
                 while (qg >= G) { qg -= G; ++qi; }
             }
         }
         cp_async_arrive(bar(B_QFULL));
-        asm volatile("bar.sync 1, 64;\n" ::: "memory");  // page ids visible to both loader warps
-        // Row-source tables: for every key row of a tile, where its K and V bytes start (nullptr = row
-        // past the end, zero-filled).  Each loader thread resolves two rows (page-table lookup), the
-        // table of the NEXT tile is built while this tile's copies are issued.
-        const char** tabK = reinterpret_cast<const char**>(gbase + OFF_TAB);   // [2][128]
-        const char** tabV = tabK + 2 * TILE_N;                                   // [2][128]
+        // Row-source tables for tiles that go through cp.async: where each key row's K and V bytes start
+        // (nullptr = row past the end, zero-filled).  Two rows per loader thread, 4 slots (tile % 4).
+        const char** tabK = reinterpret_cast<const char**>(gbase + OFF_TAB);   // [4][128]
+        const char** tabV = tabK + 4 * TILE_N;                                   // [4][128]
+        auto tile_by_tma = [&](int jj) { return a.tma_box_rows > 0 && (t0 + jj + 1) * TILE_N <= ctx; };
         auto build_table = [&](int jj) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = lt + 64 * h;
+            for (int hh = 0; hh < 2; ++hh) {
+                const int row = lt + 64 * hh;
                 const int p = (t0 + jj) * TILE_N + row;
                 const char *pk = nullptr, *pv = nullptr;
                 if (p < ctx) {
@@ -541,121 +511,107 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                         pk = kcp + o; pv = vcp + o;
                     }
                 } else if (p < total) {
-                    const int64_t r = kv0 + (p - ctx);
-                    pk = kp + ((r * a.k_rs + kvh * HD) << 1);
-                    pv = vp + ((r * a.v_rs + kvh * HD) << 1);
+                    const int64_t rr = kv0 + (p - ctx);
+                    pk = kp + ((rr * a.k_rs + kvh * HD) << 1);
+                    pv = vp + ((rr * a.v_rs + kvh * HD) << 1);
                 }
-                tabK[(jj & 1) * TILE_N + row] = pk;
-                tabV[(jj & 1) * TILE_N + row] = pv;
+                tabK[(jj & 3) * TILE_N + row] = pk;
+                tabV[(jj & 3) * TILE_N + row] = pv;
             }
         };
         auto loaders_sync = [&]() { asm volatile("bar.sync 1, 64;\n" ::: "memory"); };
-        if (!(a.tma_box_rows > 0 && (t0 + 1) * TILE_N <= ctx)) build_table(0);
-        loaders_sync();
-        bool alive = true;
-        for (int jj = 0; jj < n && alive; ++jj) {
-            const int stage = jj & 1;
-            const uint32_t par_empty = ((jj >> 1) & 1) ^ 1;
-            const bool recl = prof_thread();
-            long long cl = recl ? clock64() : 0;
-            // regular tile: all 128 keys are cached rows and the page geometry fits TMA boxes
-            const int p0 = (t0 + jj) * TILE_N;
-            const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
-            const bool next_by_tma = a.tma_box_rows > 0 && p0 + 2 * TILE_N <= ctx;
-            if (jj + 1 < n && !next_by_tma) build_table(jj + 1);
-            if (recl) { const long long c1 = clock64(); atomicAdd(&g_prof[15], (unsigned long long)(c1 - cl)); cl = c1; }
-#pragma unroll
-            for (int which = 0; which < 2; ++which) {  // 0: K tile, 1: V tile
-                bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
-                if (by_tma) {
-                    if (lt == 0) {
-                        mbar_arrive_expect_tx(full, ITEM_BYTES);
-                        const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
-                        const CUtensorMap* map = which ? &tm_v : &tm_k;
-                        const int rows = a.tma_box_rows;               // min(128, page_size)
-                        for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
-                            const int j = (p0 + r0) / a.page_size;
-                            const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
-                            const int rin = (p0 + r0) - j * a.page_size;
-                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
-                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
-                        }
-                    } else {
-                        mbar_arrive(full);
+        // issue one item (which = 0: K, 1: V) of tile jj; false when a wait gave up
+        auto issue_item = [&](int which, int jj) -> bool {
+            const int stage = which ? jj % VSTAGES : jj % KSTAGES;
+            const uint32_t par_empty = ((which ? jj / VSTAGES : jj / KSTAGES) & 1) ^ 1;
+            bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
+            if (!__all_sync(0xffffffffu, ok)) return false;
+            const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
+            const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
+            if (tile_by_tma(jj)) {
+                if (lt == 0) {
+                    mbar_arrive_expect_tx(full, ITEM_BYTES);
+                    const CUtensorMap* map = which ? &tm_v : &tm_k;
+                    const int rows = a.tma_box_rows;               // min(128, page_size)
+                    const int p0 = (t0 + jj) * TILE_N;
+                    for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
+                        const int j = (p0 + r0) / a.page_size;
+                        const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
+                        const int rin = (p0 + r0) - j * a.page_size;
+                        tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
+                        tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
                     }
                 } else {
-                    const uint32_t dbase = (which ? sV : sK) + stage * ITEM_BYTES + half_off;
-                    const char* const* tab = (which ? tabV : tabK) + stage * TILE_N;
-#pragma unroll 8
-                    for (int i = 0; i < 32; ++i) {
-                        const int row = rbase + 4 * i;
-                        const char* rp = tab[row];
-                        cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
-                    }
-                    cp_async_arrive(full);
+                    mbar_arrive(full);
                 }
-                if (recl) { const long long c1 = clock64(); atomicAdd(&g_prof[18 + which], (unsigned long long)(c1 - cl)); cl = c1; }
+            } else {
+                const uint32_t dbase = d0 + half_off;
+                const char* const* tab = (which ? tabV : tabK) + (jj & 3) * TILE_N;
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) {
+                    const int row = rbase + 4 * i;
+                    const char* rp = tab[row];
+                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
+                }
+                cp_async_arrive(full);
             }
-            loaders_sync();  // next tile's table is complete; this tile's table may be overwritten after the next sync
+            return true;
+        };
+        // Order of issue follows the order of use: K(0), K(1), then per tile V(j), K(j+2).
+        if (!tile_by_tma(0)) build_table(0);
+        if (n > 1 && !tile_by_tma(1)) build_table(1);
+        loaders_sync();
+        bool alive = issue_item(0, 0);
+        if (alive && n > 1) alive = issue_item(0, 1);
+        for (int jj = 0; jj < n && alive; ++jj) {
+            if (jj + 2 < n && !tile_by_tma(jj + 2)) build_table(jj + 2);
+            loaders_sync();  // table of tile jj + 2 complete (its slot was last read two iterations ago)
+            alive = issue_item(1, jj);
+            if (alive && jj + 2 < n) alive = issue_item(0, jj + 2);
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
     } else if (lane == 0) {
         // =========================== MMA issuer (one thread) ===========================
         constexpr uint32_t ID_QK = instr_desc(false), ID_PV = instr_desc(true);
-        auto issue_qk = [&](int t, int jj) {
-            const uint32_t kb = sK + (jj & 1) * ITEM_BYTES;
-            const uint32_t qb = sQ + t * (2 * REGION);
+        auto issue_qk = [&](int jj) {  // S[jj & 1] = Q K(jj)^T
+            const uint32_t kb = sK + (jj % KSTAGES) * ITEM_BYTES;
+            const uint32_t d = tmem + TM_S + (jj & 1) * 128;
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
-                mma_ss(tmem + t * 128, smem_desc(qb + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
+                mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
             }
         };
-        auto issue_pv = [&](int t, int jj) {
-            const uint32_t vb = sV + (jj & 1) * ITEM_BYTES;
+        auto issue_pv = [&](int jj) {  // O += P(jj) V(jj)
+            const uint32_t vb = sV + (jj % VSTAGES) * ITEM_BYTES;
+            const uint32_t pa = tmem + TM_P + (jj & 1) * 64;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-                mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV,
-                       (jj > 0 || kk > 0) ? 1u : 0u);
+                mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (jj > 0 || kk > 0) ? 1u : 0u);
         };
-        bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1) && mbar_wait(bar(B_KFULL), 0, abort_flag, 7, 0);
-        if (ok) {
-            fence_async_proxy();  // the cp.async writes (generic proxy) must be visible to the tensor pipe's reads
+        auto qk_tile = [&](int jj) -> bool {
+            if (!mbar_wait(bar(B_KFULL + jj % KSTAGES), (jj / KSTAGES) & 1, abort_flag, 10, jj)) return false;
+            fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
             tc_fence_after();
-            issue_qk(0, 0); tc_commit(bar(B_SFULL + 0));
-            if (NTILE > 1) { issue_qk(1, 0); tc_commit(bar(B_SFULL + 1)); }
-            tc_commit(bar(B_KEMPTY + 0));
-        }
+            issue_qk(jj);
+            tc_commit(bar(B_SFULL + (jj & 1)));
+            tc_commit(bar(B_KEMPTY + jj % KSTAGES));
+            return true;
+        };
+        bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1);
+        if (ok) ok = qk_tile(0);
+        if (ok && n > 1) ok = qk_tile(1);
         for (int jj = 0; jj < n && ok; ++jj) {
-            const int st = jj & 1;
-            const bool more = jj + 1 < n;
-            ok = mbar_wait(bar(B_VFULL + st), (jj >> 1) & 1, abort_flag, 8, jj) &&
-                 mbar_wait(bar(B_PFULL + 0), jj & 1, abort_flag, 9, jj);
+            ok = mbar_wait(bar(B_VFULL + jj % VSTAGES), (jj / VSTAGES) & 1, abort_flag, 8, jj) &&
+                 mbar_wait(bar(B_PFULL + (jj & 1)), (jj >> 1) & 1, abort_flag, 9, jj);
             if (!ok) break;
             fence_async_proxy();
             tc_fence_after();
-            { const bool r_ = prof_thread(); const long long c_ = r_ ? clock64() : 0; issue_pv(0, jj); if (r_) atomicAdd(&g_prof[16], (unsigned long long)(clock64() - c_)); }
-            if (more) {
-                ok = mbar_wait(bar(B_KFULL + (st ^ 1)), ((jj + 1) >> 1) & 1, abort_flag, 10, jj + 1);
-                if (!ok) break;
-                fence_async_proxy();
-                tc_fence_after();
-                { const bool r_ = prof_thread(); const long long c_ = r_ ? clock64() : 0; issue_qk(0, jj + 1); if (r_) atomicAdd(&g_prof[17], (unsigned long long)(clock64() - c_)); }
-                tc_commit(bar(B_SFULL + 0));
-            }
-            if (NTILE > 1) {
-                ok = mbar_wait(bar(B_PFULL + 1), jj & 1, abort_flag, 11, jj);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(1, jj);
-            }
-            tc_commit(bar(B_VEMPTY + st));
-            if (more) {
-                if (NTILE > 1) { issue_qk(1, jj + 1); tc_commit(bar(B_SFULL + 1)); }
-                tc_commit(bar(B_KEMPTY + (st ^ 1)));
-            }
+            issue_pv(jj);
+            tc_commit(bar(B_PVDONE));
+            tc_commit(bar(B_VEMPTY + jj % VSTAGES));
+            // S[jj & 1] was read into registers before P(jj) was written: Q K(jj+2)^T may overwrite it now
+            if (jj + 2 < n) ok = qk_tile(jj + 2);
         }
         if (ok) tc_commit(bar(B_OFULL));
     }
@@ -672,7 +628,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
 
 }  // namespace tc5
 
-bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows >= 1 && rows <= 256; }
+bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows >= 1; }
 
 // ---- TMA descriptors for the caches -----------------------------------------------------------
 // A 4-D map {head_dim, Hkv, page row, page} of one cache tensor; box {64, 1, rows, 1}, 128-byte swizzle.
@@ -756,7 +712,7 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
         if (rc != DLX_OK) return rc;
         a.tma_box_rows = rows;
     }
-    dim3 grid(a.num_splits, a.hkv, a.num_seqs), block(tc5::NUM_THREADS);
+    dim3 grid(a.num_splits, a.hkv * a.m_blocks, a.num_seqs), block(tc5::NUM_THREADS);
     tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, tm_k, tm_v);
     return check_launch("decode_attn_tc5_kernel");
 }

@@ -55,8 +55,9 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     const int64_t rows = (int64_t)group * p->max_q_len;
     d.mma = plan_mma((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
     d.use_tc5 = p->kernel != 1 && tc5_eligible((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
-    if (d.use_tc5) {  // one CTA per (sequence, KV head, split): 256 packed rows, 128-key tiles, 1 CTA/SM
-        d.mma.block_m = 256; d.mma.block_n = 64; d.mma.m_blocks = 1; d.mma.ctas_per_sm = 1;
+    if (d.use_tc5) {  // one CTA per (sequence, KV head, 128-row block, split): 128-key tiles, 1 CTA/SM
+        d.mma.block_m = 128; d.mma.block_n = 128; d.mma.ctas_per_sm = 1;
+        d.mma.m_blocks = (int)(((rows > 1 << 20 ? 1 << 20 : rows) + 127) / 128);
     }
     const int64_t max_len = p->max_kv_len > 0 ? p->max_kv_len : (int64_t)p->max_blocks * p->page_size + p->max_q_len;
     const int64_t max_tiles = (max_len + d.mma.block_n - 1) / d.mma.block_n;
