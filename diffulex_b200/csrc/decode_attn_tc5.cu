@@ -55,9 +55,15 @@ constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 4 slots x 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * 4 * TILE_N * 8;  // this sequence's page ids
 constexpr int BT_SLOTS = 3072;                     // 12 KiB: 786 k tokens at 256-token pages
-constexpr int SMEM_BYTES = OFF_BT + BT_SLOTS * 4 + 1024;  // + slack for 1024-byte alignment
-constexpr int NUM_THREADS = 224;
-constexpr int LOADER_WARP0 = 4, MMA_WARP = 6;
+constexpr int OFF_XCH = OFF_BT + BT_SLOTS * 4;     // 3 x 128 floats: row reference, two partial row sums
+constexpr int SMEM_BYTES = OFF_XCH + 3 * 128 * 4 + 1024;  // + slack for 1024-byte alignment
+// P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
+// precision however far later scores rise above m_ref, until 2^x leaves the bf16/fp32 range: a score more than
+// RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
+// device status word is set.  Earlier keys then weigh < 2^-100 of the result, far below fp32 resolution.
+#define RAISE_LIMIT 100.f
+constexpr int NUM_THREADS = 352;
+constexpr int LOADER_WARP0 = 8, MMA_WARP = 10;
 constexpr int NUM_LOADERS = 64;
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
 // TMEM columns (512): two S buffers of 128 fp32 columns, two P buffers of 64 columns (128 bf16 keys), O
@@ -70,8 +76,11 @@ enum {
     B_PFULL = 13,   // [P buffer]: the softmax may be two tiles ahead of the P V that consumes its output and an
                     // mbarrier can only be one phase ahead of its waiter, hence one barrier per buffer
     B_OFULL = 15,
-    B_PVDONE = 16,  // the latest P V has run (only waited for before a rescale of O)
-    B_COUNT = 17
+    B_MREADY = 16,  // the per-row softmax reference of the first tile is in shared memory
+    B_LSUM = 17,    // both warpgroups have published their partial row sums
+    B_SFREE = 18,   // [S buffer]: its scores are in the softmax warpgroup's registers, Q K^T may overwrite it
+    B_PFREE = 20,   // [P buffer]: the P V that read it has run, the warpgroup may write the next P into it
+    B_COUNT = 22
 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
@@ -79,8 +88,16 @@ __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] 
 // [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
 __device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
+#ifndef DLX_TC5_PROFILE
+#define DLX_TC5_PROFILE 0   // 1 compiles the cycle accounting in (it perturbs the single MMA-issuing thread)
+#endif
 __device__ __forceinline__ bool prof_thread() {
-    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && (threadIdx.x == 0 || threadIdx.x == LOADER_WARP0 * 32 || threadIdx.x == MMA_WARP * 32);
+#if DLX_TC5_PROFILE
+    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 &&
+           (threadIdx.x == 0 || threadIdx.x == LOADER_WARP0 * 32 || threadIdx.x == MMA_WARP * 32);
+#else
+    return false;
+#endif
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -305,7 +322,12 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128); }
         mbar_init(bar(B_OFULL), 1);
-        mbar_init(bar(B_PVDONE), 1);
+        mbar_init(bar(B_MREADY), 128);
+        mbar_init(bar(B_LSUM), 256);
+        mbar_init(bar(B_SFREE + 0), 128);
+        mbar_init(bar(B_SFREE + 1), 128);
+        mbar_init(bar(B_PFREE + 0), 1);
+        mbar_init(bar(B_PFREE + 1), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -319,26 +341,37 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     const uint32_t tmem = *tmem_slot;
     const long long cta_c0 = (tid == 0 && prof_thread()) ? clock64() : 0;
 
-    if (warp < 4) {
-        // =========================== softmax warpgroup ===========================
-        const int L = tid;                             // TMEM lane == row inside the tile
+    if (warp < 8) {
+        // =========================== softmax warpgroups ===========================
+        // Two warpgroups own the same 128 rows and take alternate key tiles: warpgroup w handles tiles
+        // jj = w, w + 2, ... with S buffer w and P buffer w.  One warp per SM sub-partition cannot issue
+        // fast enough to keep the MUFU unit busy; two can, and while one waits for its S the other works.
+        // Both scale their P by the SAME per-row reference m_ref = scaled row maximum of the first tile (a
+        // fixed reference is exact as long as exponents stay in range: see RAISE_LIMIT), so their outputs
+        // add up in the one O accumulator and their row sums add up at the end.
+        const int w = warp >> 2;                       // warpgroup = tile parity
+        const int L = tid & 127;                       // TMEM lane == row inside the tile
         const int r = row0 + L;                        // packed row: token r / G, head r % G
-        const bool warp_valid = warp * 32 < rows_here; // any valid row in this warp?
+        const bool warp_valid = (warp & 3) * 32 < rows_here;  // any valid row in this warp?
         const bool row_valid = L < rows_here;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        const uint32_t tO = lane_base + TM_O;
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64, tO = lane_base + TM_O;
+        float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);   // [128] m_ref, then [128] row sums of warpgroup 1
         int limit = total;
         if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = ctx + min(nnew, ((r / G) / a.dbs + 1) * a.dbs);
         const float sl2 = a.scale_log2;
-        float m_used = -INFINITY, l_run = 0.f;
+        float m_ref = 0.f, l_run = 0.f;
         bool alive = true;
-        for (int jj = 0; jj < n && alive; ++jj) {
-            const int b = jj & 1;
-            bool ok = mbar_wait(bar(B_SFULL + b), (jj >> 1) & 1, abort_flag, 1, jj);
+        if (w == 1 && n > 1) {  // the reference comes from warpgroup 0's first tile
+            bool ok = mbar_wait(bar(B_MREADY), 0, abort_flag, 4, 0);
+            alive = __all_sync(0xffffffffu, ok);
+            m_ref = xch[L];
+        }
+        for (int jj = w; jj < n && alive; jj += 2) {
+            bool ok = mbar_wait(bar(B_SFULL + w), (jj >> 1) & 1, abort_flag, 1 + w, jj);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
             if (warp_valid) {
-                const uint32_t tS = lane_base + TM_S + b * 128, tP = lane_base + TM_P + b * 64;
                 const int key0 = (t0 + jj) * TILE_N;
                 const bool rec = prof_thread();
                 long long c0 = rec ? clock64() : 0;
@@ -348,13 +381,13 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     // fully unrolled and should stay inside the instruction cache.
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t w[32];
-                        tmem_ld32(tS + c * 32, w);
+                        uint32_t wv[32];
+                        tmem_ld32(tS + c * 32, wv);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 32; ++e)
-                            if (key0 + c * 32 + e >= limit) w[e] = 0xff800000u;  // -inf
-                        tmem_st32(tS + c * 32, w);
+                            if (key0 + c * 32 + e >= limit) wv[e] = 0xff800000u;  // -inf
+                        tmem_st32(tS + c * 32, wv);
                     }
                     tmem_st_wait();
                 }
@@ -370,36 +403,41 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     for (int e = 0; e < 32; e += 2)
                         mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
                 }
-                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-                const float m_new = fmaxf(m_used, mx * sl2);
-                const bool need = (m_new > m_used) && (m_used == -INFINITY || m_new - m_used > 8.f);
-                if (__any_sync(0xffffffffu, need)) {
-                    const float alpha = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
-                    if (jj > 0) {
-                        // O holds the sum over earlier tiles: rescale it in TMEM.  P V of the previous tile may
-                        // still be running (S of THIS tile being complete only orders P V up to tile jj - 2,
-                        // because Q K^T runs two tiles ahead), so wait for it explicitly.
-                        bool ok2 = mbar_wait(bar(B_PVDONE), (jj - 1) & 1, abort_flag, 3, jj);
-                        if (!__all_sync(0xffffffffu, ok2)) { alive = false; break; }
-                        tc_fence_after();
+                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+                if (jj == 0) {  // first tile: fix the reference (0 for a row that sees nothing here)
+                    m_ref = (mx == -INFINITY) ? 0.f : mx;
+                    xch[L] = m_ref;
+                }
+                if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
+                    // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores in TMEM, flag it in
+                    // the device status word, and reload.  Rolled and rare, like the mask pre-pass.
+                    atomicOr(&g_status[0], 2);
+                    const float cap = (m_ref + RAISE_LIMIT) / sl2;
 #pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t w[32];
-                            tmem_ld32(tO + c * 32, w);
-                            tmem_ld_wait();
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t wv[32];
+                        tmem_ld32(tS + c * 32, wv);
+                        tmem_ld_wait();
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * alpha);
-                            tmem_st32(tO + c * 32, w);
-                        }
+                        for (int e = 0; e < 32; ++e) wv[e] = __float_as_uint(fminf(__uint_as_float(wv[e]), cap));
+                        tmem_st32(tS + c * 32, wv);
                     }
-                    l_run *= alpha;
-                    m_used = m_new;
+                    tmem_st_wait();
+                    tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
+                    tmem_ld_wait();
+                }
+                tc_fence_before();
+                mbar_arrive(bar(B_SFREE + w));   // S is in registers: Q K^T of tile jj + 2 may overwrite this buffer now
+                if (jj >= 2) {
+                    // Q K^T no longer waits for P V, so this warpgroup could lap the tensor pipe: P(jj - 2) must
+                    // have been consumed before P(jj) goes into the same buffer (and before this barrier's next phase)
+                    bool okp = mbar_wait(bar(B_PFREE + w), ((jj >> 1) - 1) & 1, abort_flag, 4, jj);
+                    if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
                 }
                 if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
-                const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
-                // P = exp2(s*scale - m) as bf16 into this tile's P buffer (32 keys -> 16 columns)
+                // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
                 float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
-                const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_use, -m_use);
+                const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t pk[16];
@@ -416,14 +454,31 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 l_run += lacc0.x + lacc0.y;
                 tmem_st_wait();
                 if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
+            } else {
+                // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
+                // arrival for tile jj + 2 landing in the phase of tile jj would complete that phase early.
+                mbar_arrive(bar(B_SFREE + w));
+                if (jj >= 2) {
+                    bool okp = mbar_wait(bar(B_PFREE + w), ((jj >> 1) - 1) & 1, abort_flag, 4, jj);
+                    if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                }
             }
+            if (jj == 0) mbar_arrive(bar(B_MREADY));   // m_ref of every row is in shared memory
             tc_fence_before();
-            mbar_arrive(bar(B_PFULL + b));
+            mbar_arrive(bar(B_PFULL + w));
         }
-        // ---- epilogue: O / l -> global ----
+        // ---- epilogue: O / l -> global; each warpgroup writes 64 of the 128 head_dim columns ----
         if (alive) {
-            bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 2, n);
+            bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 3, n);
             alive = __all_sync(0xffffffffu, ok);
+        }
+        if (alive) {  // the two partial row sums meet in shared memory
+            if (w == 1) xch[128 + L] = l_run; else xch[256 + L] = l_run;
+            mbar_arrive(bar(B_LSUM));
+            bool ok = mbar_wait(bar(B_LSUM), 0, abort_flag, 4, n);
+            alive = __all_sync(0xffffffffu, ok);
+            l_run += (w == 1) ? xch[256 + L] : xch[128 + L];
+            if (n == 1 && w == 1) m_ref = xch[L];
         }
         if (alive && warp_valid) {
             tc_fence_after();
@@ -431,13 +486,14 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             const int64_t tok = q0 + (row_valid ? r / G : 0);
             const int64_t head = head0 + (row_valid ? r % G : 0);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
+                const int col0 = w * 64 + c * 32;
                 uint32_t v[32];
-                tmem_ld32(tO + c * 32, v);
+                tmem_ld32(tO + col0, v);
                 tmem_ld_wait();
                 if (!row_valid) continue;
                 if (a.num_splits == 1) {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.out) + ((tok * a.o_rs + head * HD + c * 32) << 1));
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.out) + ((tok * a.o_rs + head * HD + col0) << 1));
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         uint4 o;
@@ -449,12 +505,12 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     }
                 } else {
                     const int64_t e = ((int64_t)split * a.total_q + tok) * a.hq + head;
-                    float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + c * 32);
+                    float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + col0);
 #pragma unroll
                     for (int q4 = 0; q4 < 8; ++q4)
                         dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
                                               __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
-                    if (c == 0) a.ws_lse[e] = l_run > 0.f ? m_used + log2f(l_run) : -INFINITY;
+                    if (c == 0 && w == 0) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
                 }
             }
         }
@@ -557,7 +613,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             }
             return true;
         };
-        // Order of issue follows the order of use: K(0), K(1), then per tile V(j), K(j+2).
+        // Order of issue follows the order of use: K(0), K(1), then per tile K(j+2), V(j).
         if (!tile_by_tma(0)) build_table(0);
         if (n > 1 && !tile_by_tma(1)) build_table(1);
         loaders_sync();
@@ -566,8 +622,8 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         for (int jj = 0; jj < n && alive; ++jj) {
             if (jj + 2 < n && !tile_by_tma(jj + 2)) build_table(jj + 2);
             loaders_sync();  // table of tile jj + 2 complete (its slot was last read two iterations ago)
-            alive = issue_item(1, jj);
-            if (alive && jj + 2 < n) alive = issue_item(0, jj + 2);
+            if (jj + 2 < n) alive = issue_item(0, jj + 2);
+            if (alive) alive = issue_item(1, jj);
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
     } else if (lane == 0) {
@@ -598,21 +654,36 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             tc_commit(bar(B_KEMPTY + jj % KSTAGES));
             return true;
         };
+        // Event order in steady state (the two warpgroups run half a tile apart):
+        //   S_free(0) S_free(1) P(0) S_free(2) P(1) S_free(3) P(2) ...
+        // S_free(k) lets Q K(k+2)^T overwrite S[k & 1] while tile k's exponentials are still being computed, so
+        // the next-but-one S of a warpgroup is ready before it finishes the current tile; P(k) starts P(k) V(k).
+        auto after_sfree = [&](int k) -> bool {   // Q K(k+2)^T once S(k) has been read
+            if (k + 2 >= n) return true;
+            if (!mbar_wait(bar(B_SFREE + (k & 1)), (k >> 1) & 1, abort_flag, 11, k)) return false;
+            tc_fence_after();
+            return qk_tile(k + 2);
+        };
+        auto after_p = [&](int k) -> bool {       // O += P(k) V(k)
+            if (!(mbar_wait(bar(B_VFULL + k % VSTAGES), (k / VSTAGES) & 1, abort_flag, 8, k) &&
+                  mbar_wait(bar(B_PFULL + (k & 1)), (k >> 1) & 1, abort_flag, 9, k)))
+                return false;
+            fence_async_proxy();
+            tc_fence_after();
+            issue_pv(k);
+            tc_commit(bar(B_PFREE + (k & 1)));
+            tc_commit(bar(B_VEMPTY + k % VSTAGES));
+            return true;
+        };
         bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1);
         if (ok) ok = qk_tile(0);
         if (ok && n > 1) ok = qk_tile(1);
-        for (int jj = 0; jj < n && ok; ++jj) {
-            ok = mbar_wait(bar(B_VFULL + jj % VSTAGES), (jj / VSTAGES) & 1, abort_flag, 8, jj) &&
-                 mbar_wait(bar(B_PFULL + (jj & 1)), (jj >> 1) & 1, abort_flag, 9, jj);
-            if (!ok) break;
-            fence_async_proxy();
-            tc_fence_after();
-            issue_pv(jj);
-            tc_commit(bar(B_PVDONE));
-            tc_commit(bar(B_VEMPTY + jj % VSTAGES));
-            // S[jj & 1] was read into registers before P(jj) was written: Q K(jj+2)^T may overwrite it now
-            if (jj + 2 < n) ok = qk_tile(jj + 2);
+        if (ok) ok = after_sfree(0);
+        for (int k = 1; k < n && ok; ++k) {
+            ok = after_sfree(k);
+            if (ok) ok = after_p(k - 1);
         }
+        if (ok) ok = after_p(n - 1);
         if (ok) tc_commit(bar(B_OFULL));
     }
 
