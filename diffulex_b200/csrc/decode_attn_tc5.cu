@@ -52,19 +52,19 @@ constexpr int KSTAGES = 3, VSTAGES = 2;   // Q K^T runs two tiles ahead of P V, 
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
-constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: K and V, 4 slots x 128 rows
-constexpr int OFF_BT = OFF_TAB + 2 * 4 * TILE_N * 8;  // this sequence's page ids
-constexpr int BT_SLOTS = 3072;                     // 12 KiB: 786 k tokens at 256-token pages
-constexpr int OFF_XCH = OFF_BT + BT_SLOTS * 4;     // 3 x 128 floats: row reference, two partial row sums
+constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: one per loader warp, 128 rows
+constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
+constexpr int BT_SLOTS = 2048;                     // 8 KiB each: 524 k tokens at 256-token pages
+constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 3 x 128 floats: row reference, two partial row sums
 constexpr int SMEM_BYTES = OFF_XCH + 3 * 128 * 4 + 1024;  // + slack for 1024-byte alignment
 // P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
 // precision however far later scores rise above m_ref, until 2^x leaves the bf16/fp32 range: a score more than
 // RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
 // device status word is set.  Earlier keys then weigh < 2^-100 of the result, far below fp32 resolution.
 #define RAISE_LIMIT 100.f
-constexpr int NUM_THREADS = 352;
-constexpr int LOADER_WARP0 = 8, MMA_WARP = 10;
-constexpr int NUM_LOADERS = 64;
+constexpr int NUM_THREADS = 384;
+constexpr int KLOAD_WARP = 8, VLOAD_WARP = 9, QK_WARP = 10, PV_WARP = 11;
+constexpr int NUM_LOADERS = 32;                    // lanes of one loader warp
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
 // TMEM columns (512): two S buffers of 128 fp32 columns, two P buffers of 64 columns (128 bf16 keys), O
 constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
@@ -94,7 +94,7 @@ __device__ int g_prof_on;
 __device__ __forceinline__ bool prof_thread() {
 #if DLX_TC5_PROFILE
     return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 &&
-           (threadIdx.x == 0 || threadIdx.x == LOADER_WARP0 * 32 || threadIdx.x == MMA_WARP * 32);
+           (threadIdx.x == 0 || threadIdx.x == KLOAD_WARP * 32 || threadIdx.x == QK_WARP * 32 || threadIdx.x == PV_WARP * 32);
 #else
     return false;
 #endif
@@ -266,6 +266,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
     extern __shared__ unsigned char smem_raw[];
+#if DLX_TC5_PROFILE
+    const long long t_entry = clock64();
+#define DLX_STAMP(i) do { if (prof_thread() && g_prof[i] == 0) g_prof[i] = (unsigned long long)(clock64() - t_entry); } while (0)
+#else
+#define DLX_STAMP(i) do { } while (0)
+#endif
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / a.m_blocks, mb = blockIdx.y % a.m_blocks;
     const int seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
@@ -317,7 +323,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     auto bar = [&](int slot) { return sBar + 8u * slot; };
 
     if (tid == 0) {
-        mbar_init(bar(B_QFULL), NUM_LOADERS);
+        mbar_init(bar(B_QFULL), 256);
         for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), NUM_LOADERS); mbar_init(bar(B_KEMPTY + s), 1); }
         for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128); }
@@ -331,7 +337,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (warp == MMA_WARP) {
+    if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
@@ -340,6 +346,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const long long cta_c0 = (tid == 0 && prof_thread()) ? clock64() : 0;
+    if (tid == 0) DLX_STAMP(16);
 
     if (warp < 8) {
         // =========================== softmax warpgroups ===========================
@@ -362,6 +369,23 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         const float sl2 = a.scale_log2;
         float m_ref = 0.f, l_run = 0.f;
         bool alive = true;
+        {
+            // Q: this CTA's 128 rows, loaded by the 256 softmax threads, which have nothing else to do yet (a
+            // single warp needs ~5 us for these 32 KiB of 16-byte cp.async).  Rows past the end are zero-filled;
+            // row r is token r / G, head r % G.
+            const char* qp = static_cast<const char*>(a.q);
+            const int col = tid & 15, c8 = col & 7;
+            const uint32_t half_off = (col >> 3) * REGION;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int row = (tid >> 4) + 16 * i;
+                const bool okr = row < rows_here;
+                const int rr = row0 + row;
+                const char* src = qp + (((int64_t)(q0 + rr / G) * a.q_rs + (head0 + rr % G) * HD + col * 8) << 1);
+                cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
+            }
+            cp_async_arrive(bar(B_QFULL));
+        }
         if (w == 1 && n > 1) {  // the reference comes from warpgroup 0's first tile
             bool ok = mbar_wait(bar(B_MREADY), 0, abort_flag, 4, 0);
             alive = __all_sync(0xffffffffu, ok);
@@ -371,6 +395,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             bool ok = mbar_wait(bar(B_SFULL + w), (jj >> 1) & 1, abort_flag, 1 + w, jj);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
+            if (tid == 0) DLX_STAMP(19);
             if (warp_valid) {
                 const int key0 = (t0 + jj) * TILE_N;
                 const bool rec = prof_thread();
@@ -466,11 +491,13 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             if (jj == 0) mbar_arrive(bar(B_MREADY));   // m_ref of every row is in shared memory
             tc_fence_before();
             mbar_arrive(bar(B_PFULL + w));
+            if (tid == 0) DLX_STAMP(20);
         }
         // ---- epilogue: O / l -> global; each warpgroup writes 64 of the 128 head_dim columns ----
         if (alive) {
             bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 3, n);
             alive = __all_sync(0xffffffffu, ok);
+            if (tid == 0) DLX_STAMP(22);
         }
         if (alive) {  // the two partial row sums meet in shared memory
             if (w == 1) xch[128 + L] = l_run; else xch[256 + L] = l_run;
@@ -514,82 +541,65 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 }
             }
         }
-    } else if (warp < MMA_WARP) {
-        // =========================== loaders ===========================
-        const int lt = tid - LOADER_WARP0 * 32;        // 0..63
-        const int col = lt & 15, rbase = lt >> 4;      // 16-byte chunk of the row; rows rbase + 4 i
+    } else if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
+        // =========================== loaders: one warp for Q + K tiles, one for V tiles ===========================
+        // Separate warps so that K (needed two tiles ahead by Q K^T) never queues behind a V tile that is still
+        // waiting for its ring slot.
+        const int which = warp == VLOAD_WARP;          // 0: K, 1: V
+        const int col = lane & 15, rbase = lane >> 4;  // 16-byte chunk of the row; rows rbase + 2 i
         const uint32_t half_off = (col >> 3) * REGION;
         const int c8 = col & 7;
         const char* qp = static_cast<const char*>(a.q);
-        const char* kp = static_cast<const char*>(a.k);
-        const char* vp = static_cast<const char*>(a.v);
-        const char* kcp = static_cast<const char*>(a.k_cache);
-        const char* vcp = static_cast<const char*>(a.v_cache);
+        const char* cache = static_cast<const char*>(which ? a.v_cache : a.k_cache);
+        const char* fresh = static_cast<const char*>(which ? a.v : a.k);
+        const int64_t fresh_rs = which ? a.v_rs : a.k_rs;
         const int32_t* bt_g = a.block_tables + (int64_t)seq * a.bt_stride;
-        // This sequence's page ids go to shared memory once (a per-tile global lookup would put an L2
-        // round trip in front of every tile's copies).  Longer tables than the slot fall back to global.
-        int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT);
+        // This sequence's page ids go to shared memory once (a per-tile global lookup would put an L2 round trip
+        // in front of every tile's copies); each loader warp keeps its own copy.  Longer tables fall back to global.
+        int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
         const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
         const bool bt_in_smem = pages_needed <= BT_SLOTS;
         if (bt_in_smem)
-            for (int j = lt; j < pages_needed; j += NUM_LOADERS) bt_s[j] = bt_g[j];
+            for (int j = lane; j < pages_needed; j += 32) bt_s[j] = bt_g[j];
         const int32_t* bt = bt_in_smem ? bt_s : bt_g;
-        // Q: this CTA's 128 rows, rows past the end zero-filled; row r is token r / G, head r % G, walked incrementally
-        {
-            int qi = (row0 + rbase) / G, qg = (row0 + rbase) % G;
-#pragma unroll 4
-            for (int i = 0; i < 32; ++i) {
-                const int row = rbase + 4 * i;
-                const bool okr = row < rows_here;
-                const char* src = qp + (((int64_t)(q0 + qi) * a.q_rs + (head0 + qg) * HD + col * 8) << 1);
-                cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
-                qg += 4;
-                while (qg >= G) { qg -= G; ++qi; }
-            }
-        }
-        cp_async_arrive(bar(B_QFULL));
-        // Row-source tables for tiles that go through cp.async: where each key row's K and V bytes start
-        // (nullptr = row past the end, zero-filled).  Two rows per loader thread, 4 slots (tile % 4).
-        const char** tabK = reinterpret_cast<const char**>(gbase + OFF_TAB);   // [4][128]
-        const char** tabV = tabK + 4 * TILE_N;                                   // [4][128]
-        auto tile_by_tma = [&](int jj) { return a.tma_box_rows > 0 && (t0 + jj + 1) * TILE_N <= ctx; };
-        auto build_table = [&](int jj) {
+        __syncwarp();
+        // Row-source table for tiles that go through cp.async: where each key row's bytes start (nullptr = row past
+        // the end, zero-filled).  Four rows per lane; one table per loader warp, rebuilt per tile.
+        const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
+        const int stages = which ? VSTAGES : KSTAGES;
+        bool alive = true;
+        for (int jj = 0; jj < n && alive; ++jj) {
+            const int stage = jj % stages;
+            const uint32_t par_empty = ((jj / stages) & 1) ^ 1;
+            const int p0 = (t0 + jj) * TILE_N;
+            const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
+            if (!by_tma) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int row = lt + 64 * hh;
-                const int p = (t0 + jj) * TILE_N + row;
-                const char *pk = nullptr, *pv = nullptr;
-                if (p < ctx) {
-                    const int j = p / a.page_size;
-                    const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
-                    if (pid >= 0 && pid < a.num_pages) {
-                        const int64_t o = (pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1;
-                        pk = kcp + o; pv = vcp + o;
+                for (int hh = 0; hh < 4; ++hh) {
+                    const int row = lane + 32 * hh;
+                    const int p = p0 + row;
+                    const char* ptr = nullptr;
+                    if (p < ctx) {
+                        const int j = p / a.page_size;
+                        const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
+                        if (pid >= 0 && pid < a.num_pages)
+                            ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
+                    } else if (p < total) {
+                        ptr = fresh + (((int64_t)(kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
                     }
-                } else if (p < total) {
-                    const int64_t rr = kv0 + (p - ctx);
-                    pk = kp + ((rr * a.k_rs + kvh * HD) << 1);
-                    pv = vp + ((rr * a.v_rs + kvh * HD) << 1);
+                    tab[row] = ptr;
                 }
-                tabK[(jj & 3) * TILE_N + row] = pk;
-                tabV[(jj & 3) * TILE_N + row] = pv;
+                __syncwarp();
             }
-        };
-        auto loaders_sync = [&]() { asm volatile("bar.sync 1, 64;\n" ::: "memory"); };
-        // issue one item (which = 0: K, 1: V) of tile jj; false when a wait gave up
-        auto issue_item = [&](int which, int jj) -> bool {
-            const int stage = which ? jj % VSTAGES : jj % KSTAGES;
-            const uint32_t par_empty = ((which ? jj / VSTAGES : jj / KSTAGES) & 1) ^ 1;
             bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-            if (!__all_sync(0xffffffffu, ok)) return false;
+            if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
             const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
-            if (tile_by_tma(jj)) {
-                if (lt == 0) {
+            if (by_tma) {
+                if (lane == 0) {
                     mbar_arrive_expect_tx(full, ITEM_BYTES);
                     const CUtensorMap* map = which ? &tm_v : &tm_k;
                     const int rows = a.tma_box_rows;               // min(128, page_size)
-                    const int p0 = (t0 + jj) * TILE_N;
                     for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
                         const int j = (p0 + r0) / a.page_size;
                         const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
@@ -602,96 +612,75 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 }
             } else {
                 const uint32_t dbase = d0 + half_off;
-                const char* const* tab = (which ? tabV : tabK) + (jj & 3) * TILE_N;
 #pragma unroll 8
-                for (int i = 0; i < 32; ++i) {
-                    const int row = rbase + 4 * i;
+                for (int i = 0; i < 64; ++i) {
+                    const int row = rbase + 2 * i;
                     const char* rp = tab[row];
                     cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
                 }
                 cp_async_arrive(full);
+                __syncwarp();  // the table is rebuilt for the next tile
             }
-            return true;
-        };
-        // Order of issue follows the order of use: K(0), K(1), then per tile K(j+2), V(j).
-        if (!tile_by_tma(0)) build_table(0);
-        if (n > 1 && !tile_by_tma(1)) build_table(1);
-        loaders_sync();
-        bool alive = issue_item(0, 0);
-        if (alive && n > 1) alive = issue_item(0, 1);
-        for (int jj = 0; jj < n && alive; ++jj) {
-            if (jj + 2 < n && !tile_by_tma(jj + 2)) build_table(jj + 2);
-            loaders_sync();  // table of tile jj + 2 complete (its slot was last read two iterations ago)
-            if (jj + 2 < n) alive = issue_item(0, jj + 2);
-            if (alive) alive = issue_item(1, jj);
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
-    } else if (lane == 0) {
-        // =========================== MMA issuer (one thread) ===========================
-        constexpr uint32_t ID_QK = instr_desc(false), ID_PV = instr_desc(true);
-        auto issue_qk = [&](int jj) {  // S[jj & 1] = Q K(jj)^T
-            const uint32_t kb = sK + (jj % KSTAGES) * ITEM_BYTES;
-            const uint32_t d = tmem + TM_S + (jj & 1) * 128;
+    } else if (warp == QK_WARP && lane == 0) {
+        // =========================== Q K^T issuer (one thread) ===========================
+        // S[k & 1] = Q K(k)^T.  Tiles 0 and 1 start as soon as Q and K are in; tile k + 2 starts when the softmax
+        // warpgroup has pulled S(k) into registers (S_free), i.e. while tile k's exponentials are still running.
+        constexpr uint32_t ID_QK = instr_desc(false);
+        bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1);
+        DLX_STAMP(17);
+        for (int k = 0; k < n && ok; ++k) {
+            if (k >= 2) {
+                ok = mbar_wait(bar(B_SFREE + (k & 1)), ((k - 2) >> 1) & 1, abort_flag, 11, k);
+                if (!ok) break;
+            }
+            ok = mbar_wait(bar(B_KFULL + k % KSTAGES), (k / KSTAGES) & 1, abort_flag, 10, k);
+            if (!ok) break;
+            DLX_STAMP(18);
+            fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
+            tc_fence_after();
+            const uint32_t kb = sK + (k % KSTAGES) * ITEM_BYTES;
+            const uint32_t d = tmem + TM_S + (k & 1) * 128;
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
                 mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
             }
-        };
-        auto issue_pv = [&](int jj) {  // O += P(jj) V(jj)
-            const uint32_t vb = sV + (jj % VSTAGES) * ITEM_BYTES;
-            const uint32_t pa = tmem + TM_P + (jj & 1) * 64;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-                mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (jj > 0 || kk > 0) ? 1u : 0u);
-        };
-        auto qk_tile = [&](int jj) -> bool {
-            if (!mbar_wait(bar(B_KFULL + jj % KSTAGES), (jj / KSTAGES) & 1, abort_flag, 10, jj)) return false;
-            fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
-            tc_fence_after();
-            issue_qk(jj);
-            tc_commit(bar(B_SFULL + (jj & 1)));
-            tc_commit(bar(B_KEMPTY + jj % KSTAGES));
-            return true;
-        };
-        // Event order in steady state (the two warpgroups run half a tile apart):
-        //   S_free(0) S_free(1) P(0) S_free(2) P(1) S_free(3) P(2) ...
-        // S_free(k) lets Q K(k+2)^T overwrite S[k & 1] while tile k's exponentials are still being computed, so
-        // the next-but-one S of a warpgroup is ready before it finishes the current tile; P(k) starts P(k) V(k).
-        auto after_sfree = [&](int k) -> bool {   // Q K(k+2)^T once S(k) has been read
-            if (k + 2 >= n) return true;
-            if (!mbar_wait(bar(B_SFREE + (k & 1)), (k >> 1) & 1, abort_flag, 11, k)) return false;
-            tc_fence_after();
-            return qk_tile(k + 2);
-        };
-        auto after_p = [&](int k) -> bool {       // O += P(k) V(k)
-            if (!(mbar_wait(bar(B_VFULL + k % VSTAGES), (k / VSTAGES) & 1, abort_flag, 8, k) &&
-                  mbar_wait(bar(B_PFULL + (k & 1)), (k >> 1) & 1, abort_flag, 9, k)))
-                return false;
+            tc_commit(bar(B_SFULL + (k & 1)));
+            tc_commit(bar(B_KEMPTY + k % KSTAGES));
+        }
+    } else if (warp == PV_WARP && lane == 0) {
+        // =========================== P V issuer (one thread) ===========================
+        // O += P(k) V(k), in tile order (one thread, so the accumulation order is fixed).  A second issuing
+        // thread, because tcgen05.mma issue blocks while the pipe is busy: with one thread the waits for P, K
+        // and V would line up behind each other's MMAs.
+        constexpr uint32_t ID_PV = instr_desc(true);
+        bool ok = true;
+        for (int k = 0; k < n && ok; ++k) {
+            ok = mbar_wait(bar(B_VFULL + k % VSTAGES), (k / VSTAGES) & 1, abort_flag, 8, k) &&
+                 mbar_wait(bar(B_PFULL + (k & 1)), (k >> 1) & 1, abort_flag, 9, k);
+            if (!ok) break;
             fence_async_proxy();
             tc_fence_after();
-            issue_pv(k);
+            const uint32_t vb = sV + (k % VSTAGES) * ITEM_BYTES;
+            const uint32_t pa = tmem + TM_P + (k & 1) * 64;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
+            DLX_STAMP(21);
             tc_commit(bar(B_PFREE + (k & 1)));
             tc_commit(bar(B_VEMPTY + k % VSTAGES));
-            return true;
-        };
-        bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1);
-        if (ok) ok = qk_tile(0);
-        if (ok && n > 1) ok = qk_tile(1);
-        if (ok) ok = after_sfree(0);
-        for (int k = 1; k < n && ok; ++k) {
-            ok = after_sfree(k);
-            if (ok) ok = after_p(k - 1);
         }
-        if (ok) ok = after_p(n - 1);
         if (ok) tc_commit(bar(B_OFULL));
     }
 
+    if (tid == 0) DLX_STAMP(23);
     if (tid == 0 && prof_thread()) atomicAdd(&g_prof[0], (unsigned long long)(clock64() - cta_c0));
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
-    if (warp == MMA_WARP) {
+    if (warp == QK_WARP) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem) : "memory");
     }
