@@ -56,6 +56,8 @@ _SIGNATURES = {
     "dlx_decode_attn_workspace_bytes": (c_int64, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn_num_splits": (c_int32, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
+    "dlx_static_scratch_bytes": (c_int64, []),
+    "dlx_decode_attn_static_scratch": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
     "dlx_debug_device_status": (c_int, [ctypes.POINTER(c_int32)]),
     "dlx_debug_profile": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64)]),
 }

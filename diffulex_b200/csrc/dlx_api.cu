@@ -182,3 +182,42 @@ extern "C" int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream) {
     if (d.num_splits > 1) rc = launch_combine(a, hd, st);
     return rc;
 }
+
+// ---- decode attention without any allocation by anyone ---------------------------------------------
+// Split-K scratch lives in a file-scope device array instead of caller memory.  The array's name is only
+// a host-side handle: the device address is looked up once per device with cudaGetSymbolAddress (with
+// that device current) and it is that pointer which the kernels receive.
+namespace {
+constexpr int64_t kStaticScratchBytes = 32ll << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+void* g_static_scratch_ptr[64] = {};
+}  // namespace
+
+extern "C" int64_t dlx_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+extern "C" int dlx_decode_attn_static_scratch(const dlx_decode_attn_params* p, void* stream) {
+    int rc = validate_decode(p);
+    if (rc != DLX_OK) return rc;
+    const DecodePlan d = plan_decode(p);
+    const int64_t need = d.ws_o_bytes + d.ws_lse_bytes;
+    if (need > kStaticScratchBytes)
+        return fail(DLX_ERR_WORKSPACE,
+                    "decode (static scratch): this call needs %lld scratch bytes, the built-in array holds %lld; "
+                    "lower num_splits or use dlx_decode_attn with caller memory",
+                    (long long)need, (long long)kStaticScratchBytes);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(DLX_ERR_CUDA, "decode (static scratch): cudaGetDevice: %s", cudaGetErrorString(e));
+    if (g_static_scratch_ptr[dev] == nullptr) {  // first call on this device: resolve the array's device address
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            return fail(DLX_ERR_CUDA, "decode (static scratch): cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_static_scratch_ptr[dev] = ptr;
+    }
+    dlx_decode_attn_params q = *p;
+    q.workspace = need > 0 ? g_static_scratch_ptr[dev] : nullptr;
+    q.workspace_bytes = need > 0 ? kStaticScratchBytes : 0;
+    return dlx_decode_attn(&q, stream);
+}

@@ -148,6 +148,29 @@ int32_t dlx_decode_attn_num_splits(const dlx_decode_attn_params* p);
 int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream);
 
 /*
+ * Decode attention for callers that cannot hand over scratch memory.  No counterpart in the reference.
+ *
+ * Same operator, same parameters and same results as dlx_decode_attn, but the split-K scratch (partial
+ * outputs and log-sum-exps of the key-range splits) is a fixed array inside the library's device image
+ * instead of `p->workspace` (which is ignored here).  Meant for hosts that own no allocator on the device
+ * side of the call: a serving loop whose memory pool is sized and frozen at start-up, a plugin that is
+ * handed tensors but may not call cudaMalloc (or torch's allocator) from its callback, code running
+ * under a memory budget where a late allocation failure is not an option.  The function calls no
+ * allocating routine of CUDA or of any library; q, k, v, caches, tables and `out` still come from the caller.
+ *
+ *  - Capacity: dlx_static_scratch_bytes() (32 MiB).  Every GPU that loads this library carries the array
+ *    from load to exit.  A call that would need more (see dlx_decode_attn_workspace_bytes) returns
+ *    DLX_ERR_WORKSPACE with a message and launches nothing; lower num_splits or use dlx_decode_attn.
+ *  - The first call on a device looks the array's device address up (with that device current) and keeps
+ *    it; make that first call outside of any stream capture.
+ *  - All calls on a device share the one array, which keeps whatever the last call left in it.  Nothing in
+ *    it has to start at zero: every entry a call reads was written by that call.  Two calls whose kernels
+ *    may overlap on the GPU (different streams, no dependency) race on it; order them.
+ */
+int64_t dlx_static_scratch_bytes(void);
+int dlx_decode_attn_static_scratch(const dlx_decode_attn_params* p, void* stream);
+
+/*
  * Debug aid with no counterpart in the reference.  Every wait inside the tcgen05 kernel is bounded;
  * a wait that runs out makes its CTA stop early and records {1, role, tile, cta} in a device status
  * word instead of trapping.  This call synchronises the device, copies the word to the HOST array

@@ -1,0 +1,75 @@
+"""The allocation-free decode entry point against the regular one, through the C ABI.
+
+`dlx_decode_attn_static_scratch` exists for hosts that cannot give the kernel scratch memory: a
+serving process whose device pool is carved up once at start-up, a plugin callback that is handed
+tensors but is not allowed to allocate, a caller that must not fail on a late out-of-memory.  It keeps
+the split-K scratch in a fixed 32 MiB array inside the library.  This test calls it twice in a row
+with key-range splits forced on (so the scratch is really used, and the second call runs over what the
+first one left behind) and compares with `dlx_decode_attn` fed caller-owned scratch.  Both run the same
+kernels, so the outputs are expected to be identical; the comparison still uses the attention
+tolerance of the other GPU tests.  Collected last on purpose (file name), so that a run that stops at
+the first failure has already executed every other test.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from tests.golden.cases import ATTN_CASES, attn_problem
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _params(pd, out, num_splits):
+    from diffulex_b200 import ops
+    md = pd.metadata("static")
+    return ops._decode_params(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, out, pd.block_tables, pd.context_lens,
+                              pd.cu_seqlens_q, pd.cu_seqlens_k, pd.scale, md.max_seqlen_q, 0, pd.mask_mode,
+                              pd.geometry.diffusion_block_size, num_splits)
+
+
+def test_static_scratch_entry_point_matches_regular_entry_point():
+    from diffulex_b200 import _lib
+    from oracle import attn_oracle
+    lib = _lib.lib()
+    assert torch.cuda.is_available()
+    p = attn_problem(ATTN_CASES["cfg1"])
+    pd = type(p)(**{f: (getattr(p, f).cuda() if isinstance(getattr(p, f), torch.Tensor) else getattr(p, f))
+                    for f in p.__dataclass_fields__})
+    stream = torch.cuda.current_stream().cuda_stream
+    splits = 3
+
+    # regular entry point, scratch owned by the caller
+    out_ref = torch.empty_like(pd.q)
+    pr = _params(pd, out_ref, splits)
+    need = lib.dlx_decode_attn_workspace_bytes(ctypes.byref(pr))
+    assert 0 < need <= lib.dlx_static_scratch_bytes()
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    pr.workspace, pr.workspace_bytes = ws.data_ptr(), need
+    assert lib.dlx_decode_attn(ctypes.byref(pr), stream) == 0
+
+    # allocation-free entry point, two calls in a row on the shared built-in scratch
+    outs = []
+    for _ in range(2):
+        out = torch.full_like(pd.q, float("nan"))
+        ps = _params(pd, out, splits)          # workspace fields stay NULL / 0: they are ignored
+        rc = lib.dlx_decode_attn_static_scratch(ctypes.byref(ps), stream)
+        assert rc == 0, lib.dlx_last_error().decode()
+        outs.append(out)
+    torch.cuda.synchronize()
+    for out in outs:
+        torch.testing.assert_close(out.float(), out_ref.float(), atol=ATOL, rtol=RTOL)
+    want = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
+                                        p.cu_seqlens_q, p.cu_seqlens_k, p.scale, p.mask_mode,
+                                        p.geometry.diffusion_block_size)
+    torch.testing.assert_close(outs[1].float().cpu(), want, atol=ATOL, rtol=RTOL)
+
+    # a request beyond the built-in capacity is refused with a message, nothing is launched
+    big = _params(pd, outs[0], 200)
+    big.total_q = 1 << 20   # pretend: only the size check runs before the refusal
+    assert lib.dlx_decode_attn_workspace_bytes(ctypes.byref(big)) > lib.dlx_static_scratch_bytes()
+    assert lib.dlx_decode_attn_static_scratch(ctypes.byref(big), stream) == 4
+    assert b"built-in array" in lib.dlx_last_error()
+    torch.cuda.synchronize()
