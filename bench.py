@@ -46,7 +46,7 @@ import torch
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch from the committed ncu captures
 # (profiles/), keyed by workload; None until a capture exists for that workload.
-NCU_TRAFFIC_BYTES = {}
+NCU_TRAFFIC_BYTES = {"cfg2": 178001152 + 10541824}  # profiles/decode_attn_tc5_cfg2.md
 
 
 def parse():
@@ -294,16 +294,34 @@ def main():
         h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, *h_meta.values()))
         d2h = h_out.numel() * h_out.element_size()
 
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        ev_in = [torch.cuda.Event() for _ in range(L)]
+        ev_c = [torch.cuda.Event() for _ in range(L)]
+
         def e2e_step():
-            d_q.copy_(h_q, non_blocking=True); d_k.copy_(h_k, non_blocking=True); d_v.copy_(h_v, non_blocking=True)
-            m = SimpleNamespace(**vars(md))
-            for n, t in h_meta.items():
-                setattr(m, n, t.to(dev, non_blocking=True))
+            # Three streams: host->device copies of layer i+1 run under the kernels of layer i, and the
+            # device->host copy of layer i-1's output runs under them too (PCIe is full duplex).
+            cur = torch.cuda.current_stream()
+            s_in.wait_stream(cur)
+            with torch.cuda.stream(s_in):
+                m = SimpleNamespace(**vars(md))
+                for n_, t in h_meta.items():
+                    setattr(m, n_, t.to(dev, non_blocking=True))
+                for i in range(L):
+                    d_q[i].copy_(h_q[i], non_blocking=True)
+                    d_k[i].copy_(h_k[i], non_blocking=True)
+                    d_v[i].copy_(h_v[i], non_blocking=True)
+                    ev_in[i].record(s_in)
             for i, p in enumerate(layers):
+                cur.wait_event(ev_in[i])
                 dlx.store_kvcache_unified_layout(d_k[i], d_v[i], p.k_cache, p.v_cache, m.slot_mapping, m)
                 d_out[i] = dlx.dllm_flash_attn_decode(d_q[i], d_k[i], d_v[i], p.k_cache, p.v_cache, p.scale, m)
-            h_out.copy_(d_out, non_blocking=True)
-            torch.cuda.current_stream().synchronize()  # the caller holds the result on the host
+                ev_c[i].record(cur)
+                s_out.wait_event(ev_c[i])
+                with torch.cuda.stream(s_out):
+                    h_out[i].copy_(d_out[i], non_blocking=True)
+            cur.wait_stream(s_out)
+            cur.synchronize()  # the caller holds the result on the host
 
         for _ in range(max(3, min(args.warmup, 5))):
             e2e_step()
