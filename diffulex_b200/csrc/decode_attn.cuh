@@ -20,6 +20,9 @@ struct DecodeArgs {
     int mask_mode, dbs;
     int num_splits, m_blocks;
     int tma_box_rows;  // tcgen05 kernel: rows per TMA box (0 = cached tiles are not fetched by TMA)
+    int q_tokens;      // tcgen05 kernel: whole tokens per 128-row block (128 / group)
+    int q_by_tma;      // tcgen05 kernel: Q blocks are fetched by TMA (else by 16-byte cp.async)
+    int items_total;   // tcgen05 kernel: num_seqs * hkv * m_blocks * num_splits work items, walked by persistent CTAs
     float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -34,8 +37,8 @@ MmaPlan plan_mma(int rows, int head_dim);
 int launch_decode_mma(const DecodeArgs& a, const MmaPlan& plan, int head_dim, cudaStream_t st);
 int launch_combine(const DecodeArgs& a, int head_dim, cudaStream_t st);
 
-// tcgen05 kernel: head_dim 128, 129..256 packed rows, bf16.
-bool tc5_eligible(int rows, int head_dim);
+// tcgen05 kernel: head_dim 128, up to 128 query heads per KV head, bf16.
+bool tc5_eligible(int group, int head_dim);
 int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st);
 // Copies out and clears the device status word of the tcgen05 kernel (synchronises the device).
 int read_tc5_status(int out[4]);

@@ -55,8 +55,11 @@ constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
 constexpr int BT_SLOTS = 2048;                     // 8 KiB each: 524 k tokens at 256-token pages
-constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 3 x 128 floats: row reference, two partial row sums
-constexpr int SMEM_BYTES = OFF_XCH + 3 * 128 * 4 + 1024;  // + slack for 1024-byte alignment
+constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 5 x 128 floats: row reference, 2 x 2 partial row sums
+constexpr int OFF_ITEMS = OFF_XCH + 5 * 128 * 4;   // this CTA's decoded work items, one per round
+constexpr int MAX_ROUNDS = 64;                     // more rounds than this: every role decodes its items itself
+constexpr int ITEM_SLOT = 64;                      // bytes per decoded item
+constexpr int SMEM_BYTES = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT + 1024;  // + slack for 1024-byte alignment
 // P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
 // precision however far later scores rise above m_ref, until 2^x leaves the bf16/fp32 range: a score more than
 // RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
@@ -80,7 +83,9 @@ enum {
     B_LSUM = 17,    // both warpgroups have published their partial row sums
     B_SFREE = 18,   // [S buffer]: its scores are in the softmax warpgroup's registers, Q K^T may overwrite it
     B_PFREE = 20,   // [P buffer]: the P V that read it has run, the warpgroup may write the next P into it
-    B_COUNT = 22
+    B_QEMPTY = 22,  // every Q K^T of the item has run: the next item's Q may be loaded
+    B_OFREE = 23,   // the epilogue has O in registers: the next item's P V may overwrite the accumulator
+    B_COUNT = 24
 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
@@ -88,16 +93,12 @@ __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] 
 // [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
 __device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
+__device__ unsigned long long g_tl[8 * 16];  // profile build: CTA 0's event times, [round][event]
 #ifndef DLX_TC5_PROFILE
 #define DLX_TC5_PROFILE 0   // 1 compiles the cycle accounting in (it perturbs the single MMA-issuing thread)
 #endif
 __device__ __forceinline__ bool prof_thread() {
-#if DLX_TC5_PROFILE
-    return g_prof_on && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 &&
-           (threadIdx.x == 0 || threadIdx.x == KLOAD_WARP * 32 || threadIdx.x == QK_WARP * 32 || threadIdx.x == PV_WARP * 32);
-#else
-    return false;
-#endif
+    return false;   // the per-wait cycle accounting is retired; the profile build records event times instead
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -110,15 +111,9 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n.reg .pred p;\n"
-#if DLX_WAIT_HINT
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-        "selp.b32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok) : "r"(bar), "r"(parity), "r"(DLX_WAIT_HINT) : "memory");
-#else
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
         "selp.b32 %0, 1, 0, p;\n}\n"
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-#endif
     return ok != 0;
 }
 // Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
@@ -131,9 +126,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             return true;
         }
         if ((it & 255u) == 255u && *abort_flag) return false;
-#if DLX_WAIT_SLEEP
-        if (it >= 2) __nanosleep(DLX_WAIT_SLEEP);  // a spinning warp must not eat the issue slots of the softmax warp next to it
-#endif
     }
     *abort_flag = 1;
     if (atomicCAS(&g_status[0], 0, 1) == 0) {
@@ -151,6 +143,10 @@ __device__ __forceinline__ void fence_async_proxy() { asm volatile("fence.proxy.
 __device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
+// Adds to the barrier's pending byte count without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
@@ -161,47 +157,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
 }
-#ifndef DLX_PACK_BY_ALU
-#define DLX_PACK_BY_ALU 0
-#endif
-#ifndef DLX_WAIT_HINT
-#define DLX_WAIT_HINT 0
-#endif
-#ifndef DLX_WAIT_SLEEP
-#define DLX_WAIT_SLEEP 0
-#endif
-#ifndef DLX_PINGPONG
-#define DLX_PINGPONG 1
-#endif
-#ifndef DLX_EXP_BF16X2
-#define DLX_EXP_BF16X2 0
-#endif
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
-    uint32_t y;
-    asm("ex2.approx.ftz.bf16x2 %0, %1;\n" : "=r"(y) : "r"(x));
-    return y;
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
-}
-// 2^x for a pair, on the FMA pipe: round-to-nearest split x = n + f (|f| <= 0.5) with the 1.5*2^23 magic
-// constant, 2^f by a degree-3 minimax polynomial (relative error 1.2e-4, below bf16 rounding of P), and n
-// added into the exponent field.  Inputs are clamped at -126 (2^-126 stands in for 0; -inf is a legal input).
-constexpr int POLY_PAIRS_OF_4 = 0;  // of every 4 consecutive pairs, this many use the polynomial, the rest MUFU
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    x.x = fmaxf(x.x, -126.f); x.y = fmaxf(x.y, -126.f);
-    const float2 magic = make_float2(12582912.f, 12582912.f);
-    const float2 r = __fadd2_rn(x, magic);
-    const float2 nf = __fadd2_rn(r, make_float2(-12582912.f, -12582912.f));
-    const float2 f = __ffma2_rn(nf, make_float2(-1.f, -1.f), x);
-    float2 p = __ffma2_rn(f, make_float2(0.05459282f, 0.05459282f), make_float2(0.24221784f, 0.24221784f));
-    p = __ffma2_rn(p, f, make_float2(0.69336860f, 0.69336860f));
-    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
-    p.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(r.x) << 23));
-    p.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(r.y) << 23));
-    return p;
 }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
@@ -263,57 +227,87 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
 }
 
+// One unit of work of a CTA: (sequence, KV head, block of 128 / group query tokens, key-range split), decoded from a
+// flat index.
+struct alignas(8) Item {
+    bool valid;        // has rows and at least one key tile
+    bool empty_split;  // has rows but this split's key range is empty: only -inf log-sum-exps are written
+    int seq, kvh, split;
+    int q0, ctx, kv0, nnew, total;
+    int row0, rows_here;
+    int cta_limit, full_until;
+    int t0, n;
+};
+
+__device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
+    Item it;
+    it.valid = false; it.empty_split = false;
+    it.seq = it.kvh = it.split = 0;
+    it.q0 = it.ctx = it.kv0 = it.nnew = it.total = it.row0 = it.rows_here = it.cta_limit = it.full_until = it.t0 = it.n = 0;
+    if (item < 0) return it;
+    const int per_seq = a.hkv * a.m_blocks * a.num_splits;
+    const int z = item / per_seq, rem = item - z * per_seq;
+    const int y = rem / a.num_splits;
+    it.split = rem - y * a.num_splits;
+    it.kvh = y / a.m_blocks;
+    const int mb = y - it.kvh * a.m_blocks;
+    it.seq = a.seq_order ? a.seq_order[z] : z;
+    if (it.seq < 0 || it.seq >= a.num_seqs) return it;
+    it.q0 = a.cu_q[it.seq];
+    const int qn = a.cu_q[it.seq + 1] - it.q0;
+    if (qn <= 0 || it.q0 < 0 || it.q0 + qn > a.total_q) return it;
+    it.ctx = max(a.context_lens[it.seq], 0);
+    it.kv0 = it.q0; it.nnew = qn;
+    if (a.cu_kv != nullptr) {
+        it.kv0 = a.cu_kv[it.seq];
+        it.nnew = max(a.cu_kv[it.seq + 1] - it.kv0, 0);
+    }
+    it.total = it.ctx + it.nnew;
+    // A block holds q_tokens = 128 / group whole tokens (all `group` heads of each), so that its Q rows are one box
+    // of the [token][head][head_dim] tensor; packed row r of the (sequence, KV head) is token r / group, head r % group.
+    const int tok0 = mb * a.q_tokens;
+    if (tok0 >= qn) return it;
+    it.row0 = tok0 * a.group;
+    it.rows_here = min(qn - tok0, a.q_tokens) * a.group;
+    it.cta_limit = it.full_until = it.total;
+    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
+        const int i_first = it.row0 / a.group, i_last = (it.row0 + it.rows_here - 1) / a.group;
+        it.cta_limit = it.ctx + min(it.nnew, (i_last / a.dbs + 1) * a.dbs);
+        it.full_until = it.ctx + min(it.nnew, (i_first / a.dbs + 1) * a.dbs);
+    }
+    const int n_tiles = (it.cta_limit + TILE_N - 1) / TILE_N;
+    const int tiles_per_split = (n_tiles + a.num_splits - 1) / a.num_splits;
+    it.t0 = it.split * tiles_per_split;
+    const int t1 = min(n_tiles, it.t0 + tiles_per_split);
+    if (it.t0 >= t1) { it.empty_split = true; return it; }
+    it.n = t1 - it.t0;
+    it.valid = true;
+    return it;
+}
+
+// Persistent kernel: one CTA per SM walks work items c, c + gridDim.x, ... of the (longest-first) item list.
+// Every role keeps running counters for the rings and buffers, so the pipeline never drains between items:
+// while the softmax warpgroups finish item i the loaders already fetch Q / K / V of item i + 1 and the Q K^T
+// issuer fills its first two S buffers.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k8,
+                       const __grid_constant__ CUtensorMap tm_v8) {
     extern __shared__ unsigned char smem_raw[];
 #if DLX_TC5_PROFILE
     const long long t_entry = clock64();
+    const bool tl_on = g_prof_on && blockIdx.x == 0;
 #define DLX_STAMP(i) do { if (prof_thread() && g_prof[i] == 0) g_prof[i] = (unsigned long long)(clock64() - t_entry); } while (0)
 #else
 #define DLX_STAMP(i) do { } while (0)
 #endif
-    const int split = blockIdx.x;
-    const int kvh = blockIdx.y / a.m_blocks, mb = blockIdx.y % a.m_blocks;
-    const int seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
+#if DLX_TC5_PROFILE
+#define DLX_TL(ev) do { if (tl_on && round < 8) g_tl[round * 16 + (ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
+#else
+#define DLX_TL(ev) do { } while (0)
+#endif
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.group;
-
-    // ---- CTA-uniform problem setup (before any TMEM / barrier state exists) ----
-    if (seq < 0 || seq >= a.num_seqs) return;
-    const int q0 = a.cu_q[seq];
-    const int qn = a.cu_q[seq + 1] - q0;
-    if (qn <= 0 || q0 < 0 || q0 + qn > a.total_q) return;
-    const int ctx = max(a.context_lens[seq], 0);
-    int kv0 = q0, nnew = qn;
-    if (a.cu_kv != nullptr) {
-        kv0 = a.cu_kv[seq];
-        nnew = max(a.cu_kv[seq + 1] - kv0, 0);
-    }
-    const int total = ctx + nnew;
-    const int M = qn * G;               // packed rows of this (sequence, KV head)
-    const int row0 = mb * TILE_M;       // this CTA's rows: row0 .. row0 + 127
-    if (row0 >= M) return;
-    const int rows_here = min(M - row0, TILE_M);
-    int cta_limit = total, full_until = total;
-    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
-        const int i_first = row0 / G, i_last = (row0 + rows_here - 1) / G;
-        cta_limit = ctx + min(nnew, (i_last / a.dbs + 1) * a.dbs);
-        full_until = ctx + min(nnew, (i_first / a.dbs + 1) * a.dbs);
-    }
-    const int n_tiles = (cta_limit + TILE_N - 1) / TILE_N;
-    const int tiles_per_split = (n_tiles + a.num_splits - 1) / a.num_splits;
-    const int t0 = split * tiles_per_split;
-    const int t1 = min(n_tiles, t0 + tiles_per_split);
-    const int64_t head0 = (int64_t)kvh * G;
-    if (t0 >= t1) {
-        if (a.num_splits > 1)
-            for (int r = tid; r < rows_here; r += NUM_THREADS) {
-                const int rr = row0 + r;
-                a.ws_lse[((int64_t)split * a.total_q + q0 + rr / G) * a.hq + head0 + rr % G] = -INFINITY;
-            }
-        return;
-    }
-    const int n = t1 - t0;
 
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     unsigned char* gbase = smem_raw + (sbase - smem_u32(smem_raw));
@@ -323,19 +317,50 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     auto bar = [&](int slot) { return sBar + 8u * slot; };
 
     if (tid == 0) {
-        mbar_init(bar(B_QFULL), 256);
+        mbar_init(bar(B_QFULL), a.q_by_tma ? 1 : NUM_LOADERS);
+        mbar_init(bar(B_QEMPTY), 1);
         for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), NUM_LOADERS); mbar_init(bar(B_KEMPTY + s), 1); }
         for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
-        for (int s = 0; s < 2; ++s) { mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128); }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128);
+            mbar_init(bar(B_SFREE + s), 128); mbar_init(bar(B_PFREE + s), 1);
+        }
         mbar_init(bar(B_OFULL), 1);
+        mbar_init(bar(B_OFREE), 256);
         mbar_init(bar(B_MREADY), 128);
         mbar_init(bar(B_LSUM), 256);
-        mbar_init(bar(B_SFREE + 0), 128);
-        mbar_init(bar(B_SFREE + 1), 128);
-        mbar_init(bar(B_PFREE + 0), 1);
-        mbar_init(bar(B_PFREE + 1), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    const int n_rounds = (a.items_total + (int)gridDim.x - 1) / (int)gridDim.x;
+    // Round k of the item list goes to the CTAs in alternating direction (0..G-1, then G-1..0, ...): with the list
+    // sorted longest-first this evens out the CTAs' totals, and the two row blocks of one (sequence, KV head),
+    // neighbours in the list, still run at the same time on neighbouring CTAs and share their K/V through L2.
+    auto item_of_round = [&](int k) {
+        const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+        const int item = k * (int)gridDim.x + c;
+        return item < a.items_total ? item : -1;
+    };
+    // All rounds are decoded up front, one thread per round: the chain of dependent metadata loads (sequence order ->
+    // lengths -> offsets, ~2 us) is paid once per CTA instead of once per item and role.
+    Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
+    const bool items_in_smem = n_rounds <= MAX_ROUNDS;
+    if (items_in_smem && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
+    auto get_item = [&](int k) { return items_in_smem ? items_s[k] : load_item(a, item_of_round(k)); };
+    {
+        // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
+        // by a Q box: zero them once, so that the unused TMEM lanes only ever see finite scores.
+        const int rows_used = a.q_tokens * G;
+        for (int i = tid; i < (TILE_M - rows_used) * 16; i += NUM_THREADS) {
+            const int row = rows_used + (i >> 4), chunk = i & 15;
+            *reinterpret_cast<uint4*>(gbase + (chunk >> 3) * REGION + row * 128 + ((chunk & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+        // The K and V rings start out as zeros: rows that no copy writes (past the last key of a tail tile) must hold
+        // finite values, because 0 x NaN would poison the P V product.
+        if (a.tma_box_rows > 0)
+            for (int i = tid; i < (KSTAGES + VSTAGES) * ITEM_BYTES / 16; i += NUM_THREADS)
+                *reinterpret_cast<uint4*>(gbase + OFF_K + i * 16) = make_uint4(0, 0, 0, 0);
+        fence_async_proxy();
     }
     if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
@@ -345,206 +370,226 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const long long cta_c0 = (tid == 0 && prof_thread()) ? clock64() : 0;
     if (tid == 0) DLX_STAMP(16);
+    // Running totals over the valid items this CTA has finished (identical in every role):
+    //   done = items, ck = key tiles, cb[b] = tiles that used S/P buffer b.
+    int done = 0, ck = 0, cb0 = 0, cb1 = 0;
 
     if (warp < 8) {
         // =========================== softmax warpgroups ===========================
         // Two warpgroups own the same 128 rows and take alternate key tiles: warpgroup w handles tiles
-        // jj = w, w + 2, ... with S buffer w and P buffer w.  One warp per SM sub-partition cannot issue
+        // jj = w, w + 2, ... of an item with S buffer w and P buffer w.  One warp per SM sub-partition cannot issue
         // fast enough to keep the MUFU unit busy; two can, and while one waits for its S the other works.
-        // Both scale their P by the SAME per-row reference m_ref = scaled row maximum of the first tile (a
+        // Both scale their P by the SAME per-row reference m_ref = scaled row maximum of the item's first tile (a
         // fixed reference is exact as long as exponents stay in range: see RAISE_LIMIT), so their outputs
         // add up in the one O accumulator and their row sums add up at the end.
         const int w = warp >> 2;                       // warpgroup = tile parity
         const int L = tid & 127;                       // TMEM lane == row inside the tile
-        const int r = row0 + L;                        // packed row: token r / G, head r % G
-        const bool warp_valid = (warp & 3) * 32 < rows_here;  // any valid row in this warp?
-        const bool row_valid = L < rows_here;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64, tO = lane_base + TM_O;
-        float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);   // [128] m_ref, then [128] row sums of warpgroup 1
-        int limit = total;
-        if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = ctx + min(nnew, ((r / G) / a.dbs + 1) * a.dbs);
+        float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);   // [128] m_ref, then 2 x 2 x [128] row sums (item parity, warpgroup)
         const float sl2 = a.scale_log2;
-        float m_ref = 0.f, l_run = 0.f;
         bool alive = true;
-        {
-            // Q: this CTA's 128 rows, loaded by the 256 softmax threads, which have nothing else to do yet (a
-            // single warp needs ~5 us for these 32 KiB of 16-byte cp.async).  Rows past the end are zero-filled;
-            // row r is token r / G, head r % G.
-            const char* qp = static_cast<const char*>(a.q);
-            const int col = tid & 15, c8 = col & 7;
-            const uint32_t half_off = (col >> 3) * REGION;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = (tid >> 4) + 16 * i;
-                const bool okr = row < rows_here;
-                const int rr = row0 + row;
-                const char* src = qp + (((int64_t)(q0 + rr / G) * a.q_rs + (head0 + rr % G) * HD + col * 8) << 1);
-                cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
+        for (int round = 0; round < n_rounds && alive; ++round) {
+            const Item it = get_item(round);
+            const int64_t head0 = (int64_t)it.kvh * G;
+            if (it.empty_split) {
+                if (a.num_splits > 1)
+                    for (int r = tid; r < it.rows_here; r += 256) {
+                        const int rr = it.row0 + r;
+                        a.ws_lse[((int64_t)it.split * a.total_q + it.q0 + rr / G) * a.hq + head0 + rr % G] = -INFINITY;
+                    }
+                continue;
             }
-            cp_async_arrive(bar(B_QFULL));
-        }
-        if (w == 1 && n > 1) {  // the reference comes from warpgroup 0's first tile
-            bool ok = mbar_wait(bar(B_MREADY), 0, abort_flag, 4, 0);
-            alive = __all_sync(0xffffffffu, ok);
-            m_ref = xch[L];
-        }
-        for (int jj = w; jj < n && alive; jj += 2) {
-            bool ok = mbar_wait(bar(B_SFULL + w), (jj >> 1) & 1, abort_flag, 1 + w, jj);
-            if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-            tc_fence_after();
-            if (tid == 0) DLX_STAMP(19);
-            if (warp_valid) {
-                const int key0 = (t0 + jj) * TILE_N;
-                const bool rec = prof_thread();
-                long long c0 = rec ? clock64() : 0;
-                if (key0 + TILE_N > full_until) {
-                    // The tile touches a mask boundary (warp-uniform, one or two tiles per CTA): write -inf over
-                    // the hidden scores in TMEM first.  A small rolled loop on purpose: the common path below is
-                    // fully unrolled and should stay inside the instruction cache.
+            if (!it.valid) continue;
+            const int n = it.n, rows_here = it.rows_here;
+            const int r = it.row0 + L;                     // packed row: token r / G, head r % G
+            const bool warp_valid = (warp & 3) * 32 < rows_here;  // any valid row in this warp?
+            const bool row_valid = L < rows_here;
+            const int cbw = w ? cb1 : cb0;                 // earlier uses of this warpgroup's S / P buffers
+            int limit = it.total;
+            if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = it.ctx + min(it.nnew, ((r / G) / a.dbs + 1) * a.dbs);
+            float m_ref = 0.f, l_run = 0.f;
+            if (tid == 0) DLX_TL(0);
+            if (w == 1 && n > 1) {  // the reference comes from warpgroup 0's first tile
+                bool ok = mbar_wait(bar(B_MREADY), done & 1, abort_flag, 4, 0);
+                alive = __all_sync(0xffffffffu, ok);
+                m_ref = xch[L];
+            }
+            for (int jj = w; jj < n && alive; jj += 2) {
+                const int u = cbw + (jj >> 1);             // use count of buffer w: phase of its barriers
+                bool ok = mbar_wait(bar(B_SFULL + w), u & 1, abort_flag, 1 + w, jj);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                tc_fence_after();
+                if (tid == 0) DLX_STAMP(19);
+                if (jj == w && L == 0) DLX_TL(w ? 6 : 1);
+                if (warp_valid) {
+                    const int key0 = (it.t0 + n - 1 - jj) * TILE_N;   // tiles run from the last key tile down to the first
+                    float mx_any = -INFINITY;   // first tile only: row maximum over every real key, hidden ones included
+                    if (key0 + TILE_N > it.full_until) {
+                        // The tile touches a mask boundary (warp-uniform, one or two tiles per item): write -inf over
+                        // the hidden scores in TMEM first.  A small rolled loop on purpose: the common path below is
+                        // fully unrolled and should stay inside the instruction cache.
 #pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t wv[32];
-                        tmem_ld32(tS + c * 32, wv);
-                        tmem_ld_wait();
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t wv[32];
+                            tmem_ld32(tS + c * 32, wv);
+                            tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (key0 + c * 32 + e >= limit) wv[e] = 0xff800000u;  // -inf
-                        tmem_st32(tS + c * 32, wv);
+                            for (int e = 0; e < 32; ++e) {
+                                if (jj == 0 && key0 + c * 32 + e < it.total) mx_any = fmaxf(mx_any, __uint_as_float(wv[e]));
+                                if (key0 + c * 32 + e >= limit) wv[e] = 0xff800000u;  // -inf
+                            }
+                            tmem_st32(tS + c * 32, wv);
+                        }
+                        tmem_st_wait();
                     }
-                    tmem_st_wait();
-                }
-                // the whole S row of this thread: 128 fp32 scores in registers, one TMEM round trip
-                uint32_t v[4][32];
-                tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
-                tmem_ld_wait();
-                float mx4[4];  // four independent chains: the max is latency-, not issue-bound
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    mx4[c] = -INFINITY;
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2)
-                        mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
-                }
-                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-                if (jj == 0) {  // first tile: fix the reference (0 for a row that sees nothing here)
-                    m_ref = (mx == -INFINITY) ? 0.f : mx;
-                    xch[L] = m_ref;
-                }
-                if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
-                    // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores in TMEM, flag it in
-                    // the device status word, and reload.  Rolled and rare, like the mask pre-pass.
-                    atomicOr(&g_status[0], 2);
-                    const float cap = (m_ref + RAISE_LIMIT) / sl2;
-#pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t wv[32];
-                        tmem_ld32(tS + c * 32, wv);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) wv[e] = __float_as_uint(fminf(__uint_as_float(wv[e]), cap));
-                        tmem_st32(tS + c * 32, wv);
-                    }
-                    tmem_st_wait();
+                    // the whole S row of this thread: 128 fp32 scores in registers, one TMEM round trip
+                    uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
+                    float mx4[4];  // four independent chains: the max is latency-, not issue-bound
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        mx4[c] = -INFINITY;
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2)
+                            mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
+                    }
+                    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+                    if (jj == 0) {
+                        // First tile: fix the reference.  A row that sees none of this tile's keys (block-causal rows of
+                        // an early block; the first tile is the LAST key tile) takes the maximum over the tile's hidden
+                        // keys instead: same sequence, same magnitude of scores.  0 for a padding row.
+                        m_ref = (mx != -INFINITY) ? mx : (mx_any != -INFINITY ? mx_any * sl2 : 0.f);
+                        xch[L] = m_ref;
+                        mbar_arrive(bar(B_MREADY));   // the other warpgroup needs it before its first exponential
+                    }
+                    if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
+                        // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores in TMEM, flag it in
+                        // the device status word, and reload.  Rolled and rare, like the mask pre-pass.
+                        atomicOr(&g_status[0], 2);
+                        const float cap = (m_ref + RAISE_LIMIT) / sl2;
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t wv[32];
+                            tmem_ld32(tS + c * 32, wv);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) wv[e] = __float_as_uint(fminf(__uint_as_float(wv[e]), cap));
+                            tmem_st32(tS + c * 32, wv);
+                        }
+                        tmem_st_wait();
+                        tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
+                        tmem_ld_wait();
+                    }
+                    tc_fence_before();
+                    mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
+                    if (u >= 1) {
+                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
+                        // this buffer must have been consumed before the next one goes in (and before this barrier's
+                        // next phase)
+                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                    }
+                    // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
+                    float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
+                    const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
+                            const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                            if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
+                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                        }
+                        tmem_st16(tP + c * 16, pk);
+                    }
+                    lacc0 = __fadd2_rn(lacc0, lacc1);
+                    l_run += lacc0.x + lacc0.y;
+                    tmem_st_wait();
+                } else {
+                    // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
+                    // arrival for a later tile landing in the phase of this one would complete that phase early.
+                    if (jj == 0) mbar_arrive(bar(B_MREADY));
+                    mbar_arrive(bar(B_SFREE + w));
+                    if (u >= 1) {
+                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                    }
                 }
                 tc_fence_before();
-                mbar_arrive(bar(B_SFREE + w));   // S is in registers: Q K^T of tile jj + 2 may overwrite this buffer now
-                if (jj >= 2) {
-                    // Q K^T no longer waits for P V, so this warpgroup could lap the tensor pipe: P(jj - 2) must
-                    // have been consumed before P(jj) goes into the same buffer (and before this barrier's next phase)
-                    bool okp = mbar_wait(bar(B_PFREE + w), ((jj >> 1) - 1) & 1, abort_flag, 4, jj);
-                    if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                }
-                if (rec) { const long long c1 = clock64(); atomicAdd(&g_prof[12], (unsigned long long)(c1 - c0)); c0 = c1; }
-                // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
-                float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
-                const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
-                        const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-                        if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                        pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
-                    }
-                    tmem_st16(tP + c * 16, pk);
-                }
-                lacc0 = __fadd2_rn(lacc0, lacc1);
-                l_run += lacc0.x + lacc0.y;
-                tmem_st_wait();
-                if (rec) atomicAdd(&g_prof[14], (unsigned long long)(clock64() - c0));
-            } else {
-                // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
-                // arrival for tile jj + 2 landing in the phase of tile jj would complete that phase early.
-                mbar_arrive(bar(B_SFREE + w));
-                if (jj >= 2) {
-                    bool okp = mbar_wait(bar(B_PFREE + w), ((jj >> 1) - 1) & 1, abort_flag, 4, jj);
-                    if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                }
+                mbar_arrive(bar(B_PFULL + w));
+                if (tid == 0) DLX_STAMP(20);
             }
-            if (jj == 0) mbar_arrive(bar(B_MREADY));   // m_ref of every row is in shared memory
-            tc_fence_before();
-            mbar_arrive(bar(B_PFULL + w));
-            if (tid == 0) DLX_STAMP(20);
-        }
-        // ---- epilogue: O / l -> global; each warpgroup writes 64 of the 128 head_dim columns ----
-        if (alive) {
-            bool ok = mbar_wait(bar(B_OFULL), 0, abort_flag, 3, n);
-            alive = __all_sync(0xffffffffu, ok);
-            if (tid == 0) DLX_STAMP(22);
-        }
-        if (alive) {  // the two partial row sums meet in shared memory
-            if (w == 1) xch[128 + L] = l_run; else xch[256 + L] = l_run;
-            mbar_arrive(bar(B_LSUM));
-            bool ok = mbar_wait(bar(B_LSUM), 0, abort_flag, 4, n);
-            alive = __all_sync(0xffffffffu, ok);
-            l_run += (w == 1) ? xch[256 + L] : xch[128 + L];
-            if (n == 1 && w == 1) m_ref = xch[L];
-        }
-        if (alive && warp_valid) {
-            tc_fence_after();
-            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            const int64_t tok = q0 + (row_valid ? r / G : 0);
-            const int64_t head = head0 + (row_valid ? r % G : 0);
+            // ---- epilogue: O / l -> global; each warpgroup writes 64 of the 128 head_dim columns ----
+            if (L == 0) DLX_TL(w ? 7 : 2);
+            if (alive) {  // the two partial row sums meet in shared memory, while the last P V is still running
+                float* sums = xch + 128 + (done & 1) * 256;   // double-buffered: warpgroup 0 may be an item ahead
+                sums[w * 128 + L] = l_run;
+                mbar_arrive(bar(B_LSUM));
+                bool ok = mbar_wait(bar(B_LSUM), done & 1, abort_flag, 4, n);
+                alive = __all_sync(0xffffffffu, ok);
+                l_run += sums[(w ^ 1) * 128 + L];
+                if (tid == 0) DLX_TL(3);
+            }
+            if (alive) {
+                bool ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, n);
+                alive = __all_sync(0xffffffffu, ok);
+                if (tid == 0) DLX_STAMP(22);
+                if (tid == 0) DLX_TL(4);
+            }
+            if (!alive) break;
+            if (warp_valid) {
+                tc_fence_after();
+                const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+                const int64_t tok = it.q0 + (row_valid ? r / G : 0);
+                const int64_t head = head0 + (row_valid ? r % G : 0);
 #pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-                const int col0 = w * 64 + c * 32;
-                uint32_t v[32];
-                tmem_ld32(tO + col0, v);
-                tmem_ld_wait();
-                if (!row_valid) continue;
-                if (a.num_splits == 1) {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.out) + ((tok * a.o_rs + head * HD + col0) << 1));
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        uint4 o;
-                        o.x = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 0]) * inv, __uint_as_float(v[q4 * 8 + 1]) * inv);
-                        o.y = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 2]) * inv, __uint_as_float(v[q4 * 8 + 3]) * inv);
-                        o.z = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 4]) * inv, __uint_as_float(v[q4 * 8 + 5]) * inv);
-                        o.w = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 6]) * inv, __uint_as_float(v[q4 * 8 + 7]) * inv);
-                        dst[q4] = o;
+                for (int c = 0; c < 2; ++c) {
+                    const int col0 = w * 64 + c * 32;
+                    uint32_t v[32];
+                    tmem_ld32(tO + col0, v);
+                    tmem_ld_wait();
+                    if (c == 1) {
+                        tc_fence_before();
+                        mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite the accumulator
                     }
-                } else {
-                    const int64_t e = ((int64_t)split * a.total_q + tok) * a.hq + head;
-                    float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + col0);
+                    if (!row_valid) continue;
+                    if (a.num_splits == 1) {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.out) + ((tok * a.o_rs + head * HD + col0) << 1));
 #pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4)
-                        dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
-                                              __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
-                    if (c == 0 && w == 0) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 o;
+                            o.x = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 0]) * inv, __uint_as_float(v[q4 * 8 + 1]) * inv);
+                            o.y = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 2]) * inv, __uint_as_float(v[q4 * 8 + 3]) * inv);
+                            o.z = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 4]) * inv, __uint_as_float(v[q4 * 8 + 5]) * inv);
+                            o.w = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 6]) * inv, __uint_as_float(v[q4 * 8 + 7]) * inv);
+                            dst[q4] = o;
+                        }
+                    } else {
+                        const int64_t e = ((int64_t)it.split * a.total_q + tok) * a.hq + head;
+                        float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + col0);
+#pragma unroll
+                        for (int q4 = 0; q4 < 8; ++q4)
+                            dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
+                                                  __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
+                        if (c == 0 && w == 0) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
+                    }
                 }
+            } else {
+                mbar_arrive(bar(B_OFREE));
             }
+            if (tid == 0) DLX_TL(5);
+            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
         }
     } else if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
-        // =========================== loaders: one warp for Q + K tiles, one for V tiles ===========================
+        // =========================== loaders: one warp for K tiles, one for V tiles (and later items' Q) ==========
         // Separate warps so that K (needed two tiles ahead by Q K^T) never queues behind a V tile that is still
-        // waiting for its ring slot.
+        // waiting for its ring slot.  The rings run across items: while the softmax works on the tail of one item,
+        // the first tiles of the next are already landing.
         const int which = warp == VLOAD_WARP;          // 0: K, 1: V
         const int col = lane & 15, rbase = lane >> 4;  // 16-byte chunk of the row; rows rbase + 2 i
         const uint32_t half_off = (col >> 3) * REGION;
@@ -553,102 +598,180 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         const char* cache = static_cast<const char*>(which ? a.v_cache : a.k_cache);
         const char* fresh = static_cast<const char*>(which ? a.v : a.k);
         const int64_t fresh_rs = which ? a.v_rs : a.k_rs;
-        const int32_t* bt_g = a.block_tables + (int64_t)seq * a.bt_stride;
-        // This sequence's page ids go to shared memory once (a per-tile global lookup would put an L2 round trip
-        // in front of every tile's copies); each loader warp keeps its own copy.  Longer tables fall back to global.
         int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
-        const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
-        const bool bt_in_smem = pages_needed <= BT_SLOTS;
-        if (bt_in_smem)
-            for (int j = lane; j < pages_needed; j += 32) bt_s[j] = bt_g[j];
-        const int32_t* bt = bt_in_smem ? bt_s : bt_g;
-        __syncwarp();
         // Row-source table for tiles that go through cp.async: where each key row's bytes start (nullptr = row past
         // the end, zero-filled).  Four rows per lane; one table per loader warp, rebuilt per tile.
         const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
         const int stages = which ? VSTAGES : KSTAGES;
         bool alive = true;
-        for (int jj = 0; jj < n && alive; ++jj) {
-            const int stage = jj % stages;
-            const uint32_t par_empty = ((jj / stages) & 1) ^ 1;
-            const int p0 = (t0 + jj) * TILE_N;
-            const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
-            if (!by_tma) {
-#pragma unroll
-                for (int hh = 0; hh < 4; ++hh) {
-                    const int row = lane + 32 * hh;
-                    const int p = p0 + row;
-                    const char* ptr = nullptr;
-                    if (p < ctx) {
-                        const int j = p / a.page_size;
-                        const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
-                        if (pid >= 0 && pid < a.num_pages)
-                            ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
-                    } else if (p < total) {
-                        ptr = fresh + (((int64_t)(kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
-                    }
-                    tab[row] = ptr;
+        for (int round = 0; round < n_rounds && alive; ++round) {
+            const Item it = get_item(round);
+            if (!it.valid) continue;
+            const int n = it.n, ctx = it.ctx, kvh = it.kvh;
+            const int32_t* bt_g = a.block_tables + (int64_t)it.seq * a.bt_stride;
+            // This sequence's page ids go to shared memory once per item (a per-tile global lookup would put an L2 round
+            // trip in front of every tile's copies); each loader warp keeps its own copy.  Longer tables stay global.
+            const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
+            const bool bt_in_smem = pages_needed <= BT_SLOTS;
+            __syncwarp();
+            if (bt_in_smem)
+                for (int j = lane; j < pages_needed; j += 32) bt_s[j] = bt_g[j];
+            const int32_t* bt = bt_in_smem ? bt_s : bt_g;
+            __syncwarp();
+            if (which == 1 && !a.q_by_tma) {
+                // Q without TMA (the Q K^T issuer fetches it otherwise): 16-byte cp.async as soon as the last Q K^T of
+                // the previous item has run; rows past the item's end are zero-filled.
+                if (done > 0) {
+                    bool okq = mbar_wait(bar(B_QEMPTY), (done - 1) & 1, abort_flag, 6, -2);
+                    if (!__all_sync(0xffffffffu, okq)) { alive = false; break; }
                 }
-                __syncwarp();
-            }
-            bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-            if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-            const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
-            const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
-            if (by_tma) {
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(full, ITEM_BYTES);
-                    const CUtensorMap* map = which ? &tm_v : &tm_k;
-                    const int rows = a.tma_box_rows;               // min(128, page_size)
-                    for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
-                        const int j = (p0 + r0) / a.page_size;
-                        const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
-                        const int rin = (p0 + r0) - j * a.page_size;
-                        tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
-                        tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
-                    }
-                } else {
-                    mbar_arrive(full);
-                }
-            } else {
-                const uint32_t dbase = d0 + half_off;
-#pragma unroll 8
+                const int head0 = kvh * G;
+                int qi = (it.row0 + rbase) / G, qg = (it.row0 + rbase) % G;
+#pragma unroll 4
                 for (int i = 0; i < 64; ++i) {
                     const int row = rbase + 2 * i;
-                    const char* rp = tab[row];
-                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
+                    const bool okr = row < it.rows_here;
+                    const char* src = qp + (((int64_t)(it.q0 + qi) * a.q_rs + (int64_t)(head0 + qg) * HD + col * 8) << 1);
+                    cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
+                    qg += 2;
+                    while (qg >= G) { qg -= G; ++qi; }
                 }
-                cp_async_arrive(full);
-                __syncwarp();  // the table is rebuilt for the next tile
+                cp_async_arrive(bar(B_QFULL));
             }
+            for (int jj = 0; jj < n && alive; ++jj) {
+                const int idx = ck + jj;                       // running tile count: ring position
+                const int stage = idx % stages;
+                const uint32_t par_empty = ((idx / stages) & 1) ^ 1;
+                // Key tiles are taken last-to-first: the tile with the end of the cached prefix and the in-flight rows is
+                // the slow one to fetch (row-wise copies); as an item's FIRST tile its fetch overlaps the previous item's
+                // last tiles instead of sitting at the end of the item with nothing behind it to hide it.
+                const int p0 = (it.t0 + n - 1 - jj) * TILE_N;
+                const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
+                // A tile that holds the end of the cached prefix: its leading cached rows, in whole groups of 8 (the
+                // swizzle period), still come by TMA through the 8-row map; rows [tma_rows, c_end) go through cp.async.
+                // With TMA on, rows past the last key are not written at all: they keep what an earlier tile (or the
+                // zero fill at kernel start) left there, which is finite, and their scores are masked to -inf.
+                int tma_rows = 0, c_end = TILE_N;
+                if (!by_tma && a.tma_box_rows > 0) {
+                    tma_rows = max(min(ctx - p0, TILE_N), 0) & ~7;
+                    c_end = min(it.total - p0, TILE_N);
+                }
+                if (!by_tma) {
+#pragma unroll
+                    for (int hh = 0; hh < 4; ++hh) {
+                        const int row = tma_rows + lane + 32 * hh;
+                        if (row >= c_end) break;
+                        const int p = p0 + row;
+                        const char* ptr = nullptr;
+                        if (p < ctx) {
+                            const int j = p / a.page_size;
+                            const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
+                            if (pid >= 0 && pid < a.num_pages)
+                                ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
+                        } else if (p < it.total) {
+                            ptr = fresh + (((int64_t)(it.kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
+                        }
+                        tab[row] = ptr;
+                    }
+                    __syncwarp();
+                }
+                bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
+                const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
+                if (jj == 0 && lane == 0) DLX_TL(14 + which);
+                if (by_tma) {
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(full, ITEM_BYTES);
+                        const CUtensorMap* map = which ? &tm_v : &tm_k;
+                        const int rows = a.tma_box_rows;               // min(128, page_size)
+                        for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
+                            const int j = (p0 + r0) / a.page_size;
+                            const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
+                            const int rin = (p0 + r0) - j * a.page_size;
+                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
+                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
+                        }
+                    } else {
+                        mbar_arrive(full);
+                    }
+                } else {
+                    if (tma_rows > 0 && lane == 0) {
+                        mbar_expect_tx(full, (uint32_t)tma_rows * 256u);
+                        const CUtensorMap* map = which ? &tm_v8 : &tm_k8;
+                        for (int r0 = 0; r0 < tma_rows; r0 += 8) {
+                            const int j = (p0 + r0) / a.page_size;
+                            const int pid = j < a.max_blocks ? bt[j] : -1;
+                            const int rin = (p0 + r0) - j * a.page_size;
+                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
+                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
+                        }
+                    }
+                    const uint32_t dbase = d0 + half_off;
+                    const int pairs = (c_end - tma_rows + 1) >> 1;
+#pragma unroll 4
+                    for (int i = 0; i < pairs; ++i) {
+                        const int row = tma_rows + rbase + 2 * i;
+                        if (row < c_end) {
+                            const char* rp = tab[row];
+                            cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
+                        }
+                    }
+                    cp_async_arrive(full);
+                    __syncwarp();  // the table is rebuilt for the next tile
+                }
+            }
+            ++done; ck += n;
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
     } else if (warp == QK_WARP && lane == 0) {
         // =========================== Q K^T issuer (one thread) ===========================
-        // S[k & 1] = Q K(k)^T.  Tiles 0 and 1 start as soon as Q and K are in; tile k + 2 starts when the softmax
-        // warpgroup has pulled S(k) into registers (S_free), i.e. while tile k's exponentials are still running.
+        // S[k & 1] = Q K(k)^T.  The first two tiles of an item start as soon as Q and K are in and the S buffers
+        // are free; tile k + 2 starts when the softmax warpgroup has pulled S(k) into registers (S_free), i.e.
+        // while tile k's exponentials are still running.
         constexpr uint32_t ID_QK = instr_desc(false);
-        bool ok = mbar_wait(bar(B_QFULL), 0, abort_flag, 7, -1);
-        DLX_STAMP(17);
-        for (int k = 0; k < n && ok; ++k) {
-            if (k >= 2) {
-                ok = mbar_wait(bar(B_SFREE + (k & 1)), ((k - 2) >> 1) & 1, abort_flag, 11, k);
+        bool ok = true;
+        for (int round = 0; round < n_rounds && ok; ++round) {
+            const Item it = get_item(round);
+            if (!it.valid) continue;
+            const int n = it.n;
+            if (a.q_by_tma) {
+                // Q of this item: one box per head_dim half, as soon as the last Q K^T of the previous item has run
+                // (this thread's own commit).  Tokens past the end of the tensor read as zero; tokens of the next
+                // sequence are loaded but their rows are never stored.
+                if (done > 0) ok = mbar_wait(bar(B_QEMPTY), (done - 1) & 1, abort_flag, 6, -2);
                 if (!ok) break;
+                DLX_TL(8);
+                mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
+                tma_load_3d(sQ, &tm_q, 0, it.kvh * G, it.q0 + it.row0 / G, bar(B_QFULL));
+                tma_load_3d(sQ + REGION, &tm_q, 64, it.kvh * G, it.q0 + it.row0 / G, bar(B_QFULL));
             }
-            ok = mbar_wait(bar(B_KFULL + k % KSTAGES), (k / KSTAGES) & 1, abort_flag, 10, k);
-            if (!ok) break;
-            DLX_STAMP(18);
-            fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
-            tc_fence_after();
-            const uint32_t kb = sK + (k % KSTAGES) * ITEM_BYTES;
-            const uint32_t d = tmem + TM_S + (k & 1) * 128;
+            ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
+            DLX_TL(9);
+            for (int k = 0; k < n && ok; ++k) {
+                const int u = ((k & 1) ? cb1 : cb0) + (k >> 1);   // use count of S buffer k & 1
+                if (u >= 1) {
+                    ok = mbar_wait(bar(B_SFREE + (k & 1)), (u - 1) & 1, abort_flag, 11, k);
+                    if (!ok) break;
+                }
+                const int idx = ck + k;
+                ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
+                if (!ok) break;
+                fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
+                tc_fence_after();
+                const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
+                const uint32_t d = tmem + TM_S + (k & 1) * 128;
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
-                mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
+                    mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
+                }
+                tc_commit(bar(B_SFULL + (k & 1)));
+                tc_commit(bar(B_KEMPTY + idx % KSTAGES));
             }
-            tc_commit(bar(B_SFULL + (k & 1)));
-            tc_commit(bar(B_KEMPTY + k % KSTAGES));
+            if (ok) tc_commit(bar(B_QEMPTY));   // every Q K^T of this item has read Q
+            DLX_TL(10);
+            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
         }
     } else if (warp == PV_WARP && lane == 0) {
         // =========================== P V issuer (one thread) ===========================
@@ -657,26 +780,35 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         // and V would line up behind each other's MMAs.
         constexpr uint32_t ID_PV = instr_desc(true);
         bool ok = true;
-        for (int k = 0; k < n && ok; ++k) {
-            ok = mbar_wait(bar(B_VFULL + k % VSTAGES), (k / VSTAGES) & 1, abort_flag, 8, k) &&
-                 mbar_wait(bar(B_PFULL + (k & 1)), (k >> 1) & 1, abort_flag, 9, k);
-            if (!ok) break;
-            fence_async_proxy();
-            tc_fence_after();
-            const uint32_t vb = sV + (k % VSTAGES) * ITEM_BYTES;
-            const uint32_t pa = tmem + TM_P + (k & 1) * 64;
+        for (int round = 0; round < n_rounds && ok; ++round) {
+            const Item it = get_item(round);
+            if (!it.valid) continue;
+            const int n = it.n;
+            if (done > 0) ok = mbar_wait(bar(B_OFREE), (done - 1) & 1, abort_flag, 8, -2);  // the epilogue has read O
+            DLX_TL(11);
+            for (int k = 0; k < n && ok; ++k) {
+                const int idx = ck + k;
+                const int u = ((k & 1) ? cb1 : cb0) + (k >> 1);
+                ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k) &&
+                     mbar_wait(bar(B_PFULL + (k & 1)), u & 1, abort_flag, 9, k);
+                if (!ok) break;
+                if (k == 0) DLX_TL(12);
+                fence_async_proxy();
+                tc_fence_after();
+                const uint32_t vb = sV + (idx % VSTAGES) * ITEM_BYTES;
+                const uint32_t pa = tmem + TM_P + (k & 1) * 64;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-                mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
-            DLX_STAMP(21);
-            tc_commit(bar(B_PFREE + (k & 1)));
-            tc_commit(bar(B_VEMPTY + k % VSTAGES));
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(bar(B_PFREE + (k & 1)));
+                tc_commit(bar(B_VEMPTY + idx % VSTAGES));
+            }
+            if (ok) tc_commit(bar(B_OFULL));
+            DLX_TL(13);
+            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
         }
-        if (ok) tc_commit(bar(B_OFULL));
     }
 
-    if (tid == 0) DLX_STAMP(23);
-    if (tid == 0 && prof_thread()) atomicAdd(&g_prof[0], (unsigned long long)(clock64() - cta_c0));
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
@@ -686,19 +818,20 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     }
 }
 
+static_assert(sizeof(Item) <= ITEM_SLOT, "item slot too small");
 }  // namespace tc5
 
-bool tc5_eligible(int rows, int head_dim) { return head_dim == 128 && rows >= 1; }
+bool tc5_eligible(int group, int head_dim) { return head_dim == 128 && group >= 1 && group <= 128; }
 
 // ---- TMA descriptors for the caches -----------------------------------------------------------
 // A 4-D map {head_dim, Hkv, page row, page} of one cache tensor; box {64, 1, rows, 1}, 128-byte swizzle.
 // Encoding is a host-only computation on (pointer, sizes, strides); results are memoised.
 namespace {
-struct MapKey {
-    const void* ptr; int64_t page_stride, token_stride, num_pages; int hkv, page_size, rows;
+struct MapKey {   // cache map: as named; Q map: (q, row stride, 0, total_q, Hq, group, tokens per block), rank 3
+    const void* ptr; int64_t page_stride, token_stride, num_pages; int hkv, page_size, rows; int rank = 4;
     bool operator==(const MapKey& o) const {
         return ptr == o.ptr && page_stride == o.page_stride && token_stride == o.token_stride &&
-               num_pages == o.num_pages && hkv == o.hkv && page_size == o.page_size && rows == o.rows;
+               num_pages == o.num_pages && hkv == o.hkv && page_size == o.page_size && rows == o.rows && rank == o.rank;
     }
 };
 struct MapEntry { MapKey key; CUtensorMap map; };
@@ -725,13 +858,18 @@ int cache_map(const MapKey& k, CUtensorMap* out) {
         if (e.key == k) { *out = e.map; return DLX_OK; }
     EncodeFn enc = encode_fn();
     if (enc == nullptr) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from this driver");
-    const cuuint64_t gdim[4] = {(cuuint64_t)tc5::HD, (cuuint64_t)k.hkv, (cuuint64_t)k.page_size, (cuuint64_t)k.num_pages};
-    const cuuint64_t gstr[3] = {(cuuint64_t)tc5::HD * 2, (cuuint64_t)k.token_stride * 2, (cuuint64_t)k.page_stride * 2};
-    const cuuint32_t box[4] = {64, 1, (cuuint32_t)k.rows, 1};
+    cuuint64_t gdim[4] = {(cuuint64_t)tc5::HD, (cuuint64_t)k.hkv, (cuuint64_t)k.page_size, (cuuint64_t)k.num_pages};
+    cuuint64_t gstr[3] = {(cuuint64_t)tc5::HD * 2, (cuuint64_t)k.token_stride * 2, (cuuint64_t)k.page_stride * 2};
+    cuuint32_t box[4] = {64, 1, (cuuint32_t)k.rows, 1};
+    if (k.rank == 3) {   // Q: {head_dim, Hq, token}, box {64, group, tokens per block}
+        gdim[2] = (cuuint64_t)k.num_pages;
+        gstr[1] = (cuuint64_t)k.page_stride * 2;
+        box[1] = (cuuint32_t)k.page_size; box[2] = (cuuint32_t)k.rows;
+    }
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     MapEntry e;
     e.key = k;
-    const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k.ptr), gdim, gstr, box, estr,
+    const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)k.rank, const_cast<void*>(k.ptr), gdim, gstr, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
@@ -753,9 +891,12 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
         attr_done[dev] = true;
     }
     DecodeArgs a = a_in;
-    CUtensorMap tm_k, tm_v;
+    CUtensorMap tm_k, tm_v, tm_q, tm_k8, tm_v8;
+    memset(&tm_k8, 0, sizeof(tm_k8));
+    memset(&tm_v8, 0, sizeof(tm_v8));
     memset(&tm_k, 0, sizeof(tm_k));
     memset(&tm_v, 0, sizeof(tm_v));
+    memset(&tm_q, 0, sizeof(tm_q));
     // TMA serves tiles of 128 cached keys when a tile is a whole number of equal boxes: the page size is a
     // multiple of 128 rows, or divides 128 and is a multiple of the 8-row swizzle period.
     a.tma_box_rows = 0;
@@ -767,13 +908,37 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
         const int rows = ps < 128 ? ps : 128;
         MapKey kk{a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
         MapKey kv{a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
+        MapKey kk8 = kk, kv8 = kv;   // 8-row boxes for the tile that holds the end of the cached prefix
+        kk8.rows = kv8.rows = 8;
         int rc = cache_map(kk, &tm_k);
         if (rc == DLX_OK) rc = cache_map(kv, &tm_v);
+        if (rc == DLX_OK) rc = cache_map(kk8, &tm_k8);
+        if (rc == DLX_OK) rc = cache_map(kv8, &tm_v8);
         if (rc != DLX_OK) return rc;
         a.tma_box_rows = rows;
     }
-    dim3 grid(a.num_splits, a.hkv * a.m_blocks, a.num_seqs), block(tc5::NUM_THREADS);
-    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, tm_k, tm_v);
+    // Q blocks of 128 / group whole tokens: one box {64, group, tokens} per head_dim half
+    a.q_tokens = 128 / a.group;
+    a.q_by_tma = 0;
+    if (a.total_q > 0 && a.q_rs * 2 % 16 == 0 && a.q_rs * 2 < (1ll << 40) && getenv("DLX_TC5_NO_TMA") == nullptr) {
+        MapKey kq{a.q, a.q_rs, 0, a.total_q, a.hq, a.group, a.q_tokens, 3};
+        const int rc = cache_map(kq, &tm_q);
+        if (rc != DLX_OK) return rc;
+        a.q_by_tma = 1;
+    }
+    // Persistent CTAs: one per SM (fewer when there is less work), each walks its share of the item list.
+    static int sm_count[16] = {};
+    int sms = dev < 16 ? sm_count[dev] : 0;
+    if (sms == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        if (dev < 16) sm_count[dev] = sms;
+    }
+    const int64_t items = (int64_t)a.num_seqs * a.hkv * a.m_blocks * a.num_splits;
+    if (items > (1ll << 30)) return fail(DLX_ERR_UNSUPPORTED, "decode: too many work items");
+    a.items_total = (int)items;
+    if (const char* g = getenv("DLX_TC5_GRID")) sms = atoi(g) > 0 ? atoi(g) : sms;
+    dim3 grid((unsigned)(items < sms ? items : sms)), block(tc5::NUM_THREADS);
+    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, tm_k, tm_v, tm_q, tm_k8, tm_v8);
     return check_launch("decode_attn_tc5_kernel");
 }
 
@@ -785,6 +950,15 @@ int read_tc5_status(int out[4]) {
     if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "cudaMemcpyToSymbol(g_status): %s", cudaGetErrorString(e));
     return DLX_OK;
 }
+
+#if DLX_TC5_PROFILE
+extern "C" int dlx_debug_timeline(unsigned long long* out) {   // profile build only: copies out and clears [8][16] event times
+    cudaError_t e = cudaMemcpyFromSymbol(out, tc5::g_tl, sizeof(unsigned long long) * 128);
+    unsigned long long zero[128] = {};
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_tl, zero, sizeof(zero));
+    return e == cudaSuccess ? DLX_OK : DLX_ERR_CUDA;
+}
+#endif
 
 int tc5_profile(int enable, unsigned long long out[24]) {
     cudaError_t e = cudaSuccess;

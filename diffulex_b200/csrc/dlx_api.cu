@@ -42,9 +42,8 @@ static int validate_decode(const dlx_decode_attn_params* p) {
     if (p->num_splits < 0 || p->num_splits > 256) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: num_splits %d", p->num_splits);
     if (!(p->scale > 0.f) || !isfinite(p->scale)) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: scale must be positive and finite");
     if (p->kernel < 0 || p->kernel > 2) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: kernel %d", p->kernel);
-    if (p->kernel == 2 && !tc5_eligible((int)((int64_t)(p->num_q_heads / p->num_kv_heads) * p->max_q_len > 1 << 20
-                                                  ? 1 << 20 : (p->num_q_heads / p->num_kv_heads) * p->max_q_len), p->head_dim))
-        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernel serves head_dim 128 with up to 256 packed rows");
+    if (p->kernel == 2 && !tc5_eligible(p->num_q_heads / p->num_kv_heads, p->head_dim))
+        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernel serves head_dim 128 with up to 128 query heads per KV head");
     if (p->num_seqs > 65535) return fail(DLX_ERR_UNSUPPORTED, "decode: more than 65535 sequences per call");
     return DLX_OK;
 }
@@ -54,10 +53,12 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     const int group = p->num_q_heads / p->num_kv_heads;
     const int64_t rows = (int64_t)group * p->max_q_len;
     d.mma = plan_mma((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
-    d.use_tc5 = p->kernel != 1 && tc5_eligible((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
-    if (d.use_tc5) {  // one CTA per (sequence, KV head, 128-row block, split): 128-key tiles, 1 CTA/SM
+    d.use_tc5 = p->kernel != 1 && tc5_eligible(group, p->head_dim);
+    if (d.use_tc5) {  // work item = (sequence, KV head, block of 128 / group whole tokens, split): 128-key tiles, 1 CTA/SM
         d.mma.block_m = 128; d.mma.block_n = 128; d.mma.ctas_per_sm = 1;
-        d.mma.m_blocks = (int)(((rows > 1 << 20 ? 1 << 20 : rows) + 127) / 128);
+        const int tokens_per_block = 128 / group;
+        const int q_len = p->max_q_len > 1 << 20 ? 1 << 20 : p->max_q_len;
+        d.mma.m_blocks = (q_len + tokens_per_block - 1) / tokens_per_block;
     }
     const int64_t max_len = p->max_kv_len > 0 ? p->max_kv_len : (int64_t)p->max_blocks * p->page_size + p->max_q_len;
     const int64_t max_tiles = (max_len + d.mma.block_n - 1) / d.mma.block_n;
