@@ -54,12 +54,18 @@ constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
-constexpr int BT_SLOTS = 2048;                     // 8 KiB each: 524 k tokens at 256-token pages
-constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 5 x 128 floats: row reference, 2 x 2 partial row sums
-constexpr int OFF_ITEMS = OFF_XCH + 5 * 128 * 4;   // this CTA's decoded work items, one per round
+constexpr int BT_SLOTS = 1024;                     // 4 KiB each: 262 k tokens at 256-token pages
+constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 4 x 128 floats: two slots of row references, two of partial row sums
+constexpr int OFF_STAGE = OFF_XCH + 4 * 128 * 4;   // output staging: 32 rows x 64 bytes per softmax warp
+constexpr int STAGE_WARP_BYTES = 32 * 64;
+constexpr int OFF_ROWMAP = OFF_STAGE + 8 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group) of a block's rows
+constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;   // this CTA's decoded work items, one per round
 constexpr int MAX_ROUNDS = 64;                     // more rounds than this: every role decodes its items itself
 constexpr int ITEM_SLOT = 64;                      // bytes per decoded item
-constexpr int SMEM_BYTES = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT + 1024;  // + slack for 1024-byte alignment
+constexpr int OFF_ARGS = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT;   // a copy of the argument block (256 bytes)
+constexpr int SMEM_BYTES = OFF_ARGS + 256 + 1024;  // + slack for 1024-byte alignment
+static_assert(sizeof(DecodeArgs) <= 256, "argument block copy");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 // P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
 // precision however far later scores rise above m_ref, until 2^x leaves the bf16/fp32 range: a score more than
 // RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
@@ -79,13 +85,16 @@ enum {
     B_PFULL = 13,   // [P buffer]: the softmax may be two tiles ahead of the P V that consumes its output and an
                     // mbarrier can only be one phase ahead of its waiter, hence one barrier per buffer
     B_OFULL = 15,
-    B_MREADY = 16,  // the per-row softmax reference of the first tile is in shared memory
-    B_LSUM = 17,    // both warpgroups have published their partial row sums
+    B_OFREE = 16,   // the epilogue has O in registers: the next item's P V may overwrite the accumulator
+    B_QEMPTY = 17,  // every Q K^T of the item has run: the next item's Q may be loaded
     B_SFREE = 18,   // [S buffer]: its scores are in the softmax warpgroup's registers, Q K^T may overwrite it
     B_PFREE = 20,   // [P buffer]: the P V that read it has run, the warpgroup may write the next P into it
-    B_QEMPTY = 22,  // every Q K^T of the item has run: the next item's Q may be loaded
-    B_OFREE = 23,   // the epilogue has O in registers: the next item's P V may overwrite the accumulator
-    B_COUNT = 24
+    // Rings of two slots between the warpgroups, one use per item with two or more tiles:
+    B_MRFULL = 22,  // [slot] the row references of the item's first tile are in shared memory
+    B_MREMPTY = 24, // [slot] ... and have been read by the owner of the item's second tile
+    B_LSFULL = 26,  // [slot] the partial row sums of the warpgroup that does not write the item's output are in
+    B_LSEMPTY = 28, // [slot] ... and have been added by the one that does
+    B_COUNT = 30
 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
@@ -93,7 +102,7 @@ __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] 
 // [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
 __device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
-__device__ unsigned long long g_tl[8 * 16];  // profile build: CTA 0's event times, [round][event]
+__device__ unsigned long long g_tl[8 * 24];  // profile build: CTA 0's event times, [round][event]
 #ifndef DLX_TC5_PROFILE
 #define DLX_TC5_PROFILE 0   // 1 compiles the cycle accounting in (it perturbs the single MMA-issuing thread)
 #endif
@@ -116,23 +125,24 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
-    const bool rec = prof_thread();
-    const long long c0 = rec ? clock64() : 0;
+// Slow half of a bounded wait, out of line (there are ~40 wait sites): keeps polling up to the limit, gives up early when
+// another thread of the CTA has, and on expiry raises the CTA's abort flag and records (site, tile, CTA).
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
     for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
-        if (mbar_try(bar, parity)) {
-            if (rec) atomicAdd(&g_prof[role], (unsigned long long)(clock64() - c0));
-            return true;
-        }
+        if (mbar_try(bar, parity)) return true;
         if ((it & 255u) == 255u && *abort_flag) return false;
     }
     *abort_flag = 1;
     if (atomicCAS(&g_status[0], 0, 1) == 0) {
         g_status[1] = role; g_status[2] = tile;
-        g_status[3] = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+        g_status[3] = blockIdx.x;
     }
     return false;
+}
+// Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
+    if (mbar_try(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, abort_flag, role, tile);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
@@ -234,16 +244,17 @@ struct alignas(8) Item {
     bool empty_split;  // has rows but this split's key range is empty: only -inf log-sum-exps are written
     int seq, kvh, split;
     int q0, ctx, kv0, nnew, total;
-    int row0, rows_here;
+    int row0, rows_here, tok0;   // first packed row (= tok0 * group), valid rows, first token of the block
     int cta_limit, full_until;
     int t0, n;
 };
 
-__device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
+// Not inlined: five call sites, ~3 KB of code each, and instruction-cache room is what the per-item code paths lack.
+__device__ __noinline__ Item load_item(const DecodeArgs& a, int item) {
     Item it;
     it.valid = false; it.empty_split = false;
     it.seq = it.kvh = it.split = 0;
-    it.q0 = it.ctx = it.kv0 = it.nnew = it.total = it.row0 = it.rows_here = it.cta_limit = it.full_until = it.t0 = it.n = 0;
+    it.q0 = it.ctx = it.kv0 = it.nnew = it.total = it.row0 = it.rows_here = it.tok0 = it.cta_limit = it.full_until = it.t0 = it.n = 0;
     if (item < 0) return it;
     const int per_seq = a.hkv * a.m_blocks * a.num_splits;
     const int z = item / per_seq, rem = item - z * per_seq;
@@ -268,6 +279,7 @@ __device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
     const int tok0 = mb * a.q_tokens;
     if (tok0 >= qn) return it;
     it.row0 = tok0 * a.group;
+    it.tok0 = tok0;
     it.rows_here = min(qn - tok0, a.q_tokens) * a.group;
     it.cta_limit = it.full_until = it.total;
     if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
@@ -285,12 +297,19 @@ __device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
     return it;
 }
 
+// Order of an item's n key tiles: n-2, n-1, n-3, n-4, ..., 0.  The last tile (end of the cached prefix plus the
+// in-flight rows) is the slow one to fetch (row-wise copies) and needs the mask pre-pass: near the front, its fetch
+// overlaps the previous item's last tiles instead of sitting at the item's end with nothing behind it to hide it.
+// It is not the very first, because the first tile's row maxima become the softmax reference that the other
+// warpgroup waits for: a full tile delivers them sooner, while the other warpgroup masks the last tile.
+__device__ __forceinline__ int tile_of(int jj, int n) { return n - 1 - ((jj < 2 && n >= 2) ? (jj ^ 1) : jj); }
+
 // Persistent kernel: one CTA per SM walks work items c, c + gridDim.x, ... of the (longest-first) item list.
 // Every role keeps running counters for the rings and buffers, so the pipeline never drains between items:
 // while the softmax warpgroups finish item i the loaders already fetch Q / K / V of item i + 1 and the Q K^T
 // issuer fills its first two S buffers.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k8,
                        const __grid_constant__ CUtensorMap tm_v8) {
     extern __shared__ unsigned char smem_raw[];
@@ -302,12 +321,11 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
 #define DLX_STAMP(i) do { } while (0)
 #endif
 #if DLX_TC5_PROFILE
-#define DLX_TL(ev) do { if (tl_on && round < 8) g_tl[round * 16 + (ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
+#define DLX_TL(ev) do { if (tl_on && round < 8) g_tl[round * 24 + (ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
 #else
 #define DLX_TL(ev) do { } while (0)
 #endif
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = a.group;
 
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     unsigned char* gbase = smem_raw + (sbase - smem_u32(smem_raw));
@@ -315,6 +333,17 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * B_COUNT);
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT + 8);
     auto bar = [&](int slot) { return sBar + 8u * slot; };
+    // The argument block is read from a shared-memory copy: fields that only the per-item code touches (output
+    // pointer, strides, mask mode ...) fall out of the constant cache between items, and every such miss was a trip
+    // to L2 in the middle of an item switch.
+    {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&a_param);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(gbase + OFF_ARGS);
+        if (tid < (int)(sizeof(DecodeArgs) / 4)) dst[tid] = src[tid];
+        __syncthreads();
+    }
+    const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);
+    const int G = a.group;
 
     if (tid == 0) {
         mbar_init(bar(B_QFULL), a.q_by_tma ? 1 : NUM_LOADERS);
@@ -326,9 +355,11 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
             mbar_init(bar(B_SFREE + s), 128); mbar_init(bar(B_PFREE + s), 1);
         }
         mbar_init(bar(B_OFULL), 1);
-        mbar_init(bar(B_OFREE), 256);
-        mbar_init(bar(B_MREADY), 128);
-        mbar_init(bar(B_LSUM), 256);
+        mbar_init(bar(B_OFREE), 128);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar(B_MRFULL + s), 128); mbar_init(bar(B_MREMPTY + s), 128);
+            mbar_init(bar(B_LSFULL + s), 128); mbar_init(bar(B_LSEMPTY + s), 128);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -346,6 +377,10 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
     const bool items_in_smem = n_rounds <= MAX_ROUNDS;
     if (items_in_smem && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
+    // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
+    // row index into (token, head) is the same for every item and is tabulated once.
+    int2* rowmap = reinterpret_cast<int2*>(gbase + OFF_ROWMAP);
+    if (tid >= 128 && tid < 256) rowmap[tid - 128] = make_int2((tid - 128) / G, (tid - 128) % G);
     auto get_item = [&](int k) { return items_in_smem ? items_s[k] : load_item(a, item_of_round(k)); };
     {
         // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
@@ -372,59 +407,72 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
     const uint32_t tmem = *tmem_slot;
     if (tid == 0) DLX_STAMP(16);
     // Running totals over the valid items this CTA has finished (identical in every role):
-    //   done = items, ck = key tiles, cb[b] = tiles that used S/P buffer b.
-    int done = 0, ck = 0, cb0 = 0, cb1 = 0;
+    //   done = items, ck = key tiles.  Tile k of an item has running index ck + k: S/P buffer (ck + k) & 1, and
+    //   (ck + k) >> 1 earlier uses of that buffer.
+    int done = 0, ck = 0;
 
     if (warp < 8) {
         // =========================== softmax warpgroups ===========================
-        // Two warpgroups own the same 128 rows and take alternate key tiles: warpgroup w handles tiles
-        // jj = w, w + 2, ... of an item with S buffer w and P buffer w.  One warp per SM sub-partition cannot issue
-        // fast enough to keep the MUFU unit busy; two can, and while one waits for its S the other works.
-        // Both scale their P by the SAME per-row reference m_ref = scaled row maximum of the item's first tile (a
-        // fixed reference is exact as long as exponents stay in range: see RAISE_LIMIT), so their outputs
-        // add up in the one O accumulator and their row sums add up at the end.
-        const int w = warp >> 2;                       // warpgroup = tile parity
+        // Two warpgroups own the same 128 rows (thread = row = TMEM lane) and take alternate key tiles, counted ACROSS
+        // items: the tile with running index g belongs to warpgroup g & 1, which always works on S buffer / P buffer
+        // g & 1.  One warp per SM sub-partition cannot issue fast enough to keep the MUFU unit busy; two can, and
+        // while one waits for its S the other works.  Both scale their P by the SAME per-row reference m_ref = scaled
+        // row maximum of the item's first tile (a fixed reference is exact as long as exponents stay in range: see
+        // RAISE_LIMIT), so their outputs add up in the one O accumulator and their row sums add up at the end.
+        // The warpgroup that owns an item's last tile writes the item's output; the other one is by then already
+        // working on the next item's first tile, whose S is waiting in TMEM.
+        const int w = warp >> 2;                       // warpgroup = parity of the running tile index
         const int L = tid & 127;                       // TMEM lane == row inside the tile
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64, tO = lane_base + TM_O;
-        float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);   // [128] m_ref, then 2 x 2 x [128] row sums (item parity, warpgroup)
+        float* xm = reinterpret_cast<float*>(gbase + OFF_XCH);    // [2][128] row references, ring of two items
+        float* xs = xm + 256;                                     // [2][128] partial row sums, ring of two items
+        unsigned char* stage = gbase + OFF_STAGE + warp * STAGE_WARP_BYTES;   // output staging of this warp
         const float sl2 = a.scale_log2;
+        int mr = 0;                                    // items with two or more tiles so far: position in both rings
         bool alive = true;
+#pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
+            if (L == 0) DLX_TL(w ? 20 : 19);
             const Item it = get_item(round);
             const int64_t head0 = (int64_t)it.kvh * G;
             if (it.empty_split) {
                 if (a.num_splits > 1)
                     for (int r = tid; r < it.rows_here; r += 256) {
-                        const int rr = it.row0 + r;
-                        a.ws_lse[((int64_t)it.split * a.total_q + it.q0 + rr / G) * a.hq + head0 + rr % G] = -INFINITY;
+                        const int2 dm = rowmap[r];
+                        a.ws_lse[((int64_t)it.split * a.total_q + it.q0 + it.tok0 + dm.x) * a.hq + head0 + dm.y] = -INFINITY;
                     }
                 continue;
             }
             if (!it.valid) continue;
             const int n = it.n, rows_here = it.rows_here;
-            const int r = it.row0 + L;                     // packed row: token r / G, head r % G
+            const int2 my_row = rowmap[L];                 // packed row L of the block: token tok0 + x, head head0 + y
             const bool warp_valid = (warp & 3) * 32 < rows_here;  // any valid row in this warp?
             const bool row_valid = L < rows_here;
-            const int cbw = w ? cb1 : cb0;                 // earlier uses of this warpgroup's S / P buffers
+            const int jj_first = (w ^ ck) & 1;             // this warpgroup's first tile of the item (0 or 1)
+            const bool writer = ((ck + n - 1) & 1) == w;   // owns the last tile: runs the epilogue
+            const bool multi = n >= 2;                     // both warpgroups have tiles: reference and sums are exchanged
+            const int slot = mr & 1;
+            const uint32_t ring_par = (mr >> 1) & 1;
             int limit = it.total;
-            if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = it.ctx + min(it.nnew, ((r / G) / a.dbs + 1) * a.dbs);
+            if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = it.ctx + min(it.nnew, ((it.tok0 + my_row.x) / a.dbs + 1) * a.dbs);
             float m_ref = 0.f, l_run = 0.f;
             if (tid == 0) DLX_TL(0);
-            if (w == 1 && n > 1) {  // the reference comes from warpgroup 0's first tile
-                bool ok = mbar_wait(bar(B_MREADY), done & 1, abort_flag, 4, 0);
-                alive = __all_sync(0xffffffffu, ok);
-                m_ref = xch[L];
-            }
-            for (int jj = w; jj < n && alive; jj += 2) {
-                const int u = cbw + (jj >> 1);             // use count of buffer w: phase of its barriers
+#pragma unroll 1
+            for (int jj = jj_first; jj < n && alive; jj += 2) {
+                const int u = (ck + jj) >> 1;              // use count of this warpgroup's buffers: phase of their barriers
                 bool ok = mbar_wait(bar(B_SFULL + w), u & 1, abort_flag, 1 + w, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
-                if (tid == 0) DLX_STAMP(19);
-                if (jj == w && L == 0) DLX_TL(w ? 6 : 1);
+                if (jj == jj_first && L == 0) DLX_TL(w ? 6 : 1);
+                // Ring bookkeeping of the row reference (all warps, valid rows or not, keep the barrier counts whole):
+                // the owner of tile 0 fills the slot, the owner of tile 1 drains it.
+                if (multi && jj == 0 && mr >= 2) {
+                    bool oke = mbar_wait(bar(B_MREMPTY + slot), ring_par ^ 1, abort_flag, 4, -3);
+                    if (!__all_sync(0xffffffffu, oke)) { alive = false; break; }
+                }
                 if (warp_valid) {
-                    const int key0 = (it.t0 + n - 1 - jj) * TILE_N;   // tiles run from the last key tile down to the first
+                    const int key0 = (it.t0 + tile_of(jj, n)) * TILE_N;
                     float mx_any = -INFINITY;   // first tile only: row maximum over every real key, hidden ones included
                     if (key0 + TILE_N > it.full_until) {
                         // The tile touches a mask boundary (warp-uniform, one or two tiles per item): write -inf over
@@ -459,11 +507,18 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
                     if (jj == 0) {
                         // First tile: fix the reference.  A row that sees none of this tile's keys (block-causal rows of
-                        // an early block; the first tile is the LAST key tile) takes the maximum over the tile's hidden
+                        // an early block; the first tile is a late key tile) takes the maximum over the tile's hidden
                         // keys instead: same sequence, same magnitude of scores.  0 for a padding row.
                         m_ref = (mx != -INFINITY) ? mx : (mx_any != -INFINITY ? mx_any * sl2 : 0.f);
-                        xch[L] = m_ref;
-                        mbar_arrive(bar(B_MREADY));   // the other warpgroup needs it before its first exponential
+                        if (multi) {
+                            xm[slot * 128 + L] = m_ref;
+                            mbar_arrive(bar(B_MRFULL + slot));   // the other warpgroup needs it before its first exponential
+                        }
+                    } else if (jj == 1) {  // the other warpgroup's first tile set the reference
+                        bool okm = mbar_wait(bar(B_MRFULL + slot), ring_par, abort_flag, 4, 0);
+                        if (!__all_sync(0xffffffffu, okm)) { alive = false; break; }
+                        m_ref = xm[slot * 128 + L];
+                        mbar_arrive(bar(B_MREMPTY + slot));
                     }
                     if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
                         // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores in TMEM, flag it in
@@ -513,77 +568,128 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 } else {
                     // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
                     // arrival for a later tile landing in the phase of this one would complete that phase early.
-                    if (jj == 0) mbar_arrive(bar(B_MREADY));
+                    if (multi && jj == 0) mbar_arrive(bar(B_MRFULL + slot));
+                    if (jj == 1) {
+                        bool okm = mbar_wait(bar(B_MRFULL + slot), ring_par, abort_flag, 4, 0);
+                        if (!__all_sync(0xffffffffu, okm)) { alive = false; break; }
+                        mbar_arrive(bar(B_MREMPTY + slot));
+                    }
                     mbar_arrive(bar(B_SFREE + w));
                     if (u >= 1) {
                         bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
                         if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
                     }
                 }
+                if (jj == n - 1 && done >= 1) {
+                    // This warpgroup will wait for the item's O_full next.  It may not have watched the previous item's
+                    // (the other warpgroup wrote that one), and a parity wait can only tell the current phase from the
+                    // one before: make sure the previous phase is over while this item's cannot complete yet.
+                    bool oko = mbar_wait(bar(B_OFULL), (done - 1) & 1, abort_flag, 3, -6);
+                    if (!__all_sync(0xffffffffu, oko)) { alive = false; break; }
+                }
                 tc_fence_before();
                 mbar_arrive(bar(B_PFULL + w));
-                if (tid == 0) DLX_STAMP(20);
             }
-            // ---- epilogue: O / l -> global; each warpgroup writes 64 of the 128 head_dim columns ----
             if (L == 0) DLX_TL(w ? 7 : 2);
-            if (alive) {  // the two partial row sums meet in shared memory, while the last P V is still running
-                float* sums = xch + 128 + (done & 1) * 256;   // double-buffered: warpgroup 0 may be an item ahead
-                sums[w * 128 + L] = l_run;
-                mbar_arrive(bar(B_LSUM));
-                bool ok = mbar_wait(bar(B_LSUM), done & 1, abort_flag, 4, n);
-                alive = __all_sync(0xffffffffu, ok);
-                l_run += sums[(w ^ 1) * 128 + L];
-                if (tid == 0) DLX_TL(3);
-            }
-            if (alive) {
-                bool ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, n);
-                alive = __all_sync(0xffffffffu, ok);
-                if (tid == 0) DLX_STAMP(22);
-                if (tid == 0) DLX_TL(4);
-            }
             if (!alive) break;
-            if (warp_valid) {
-                tc_fence_after();
-                const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-                const int64_t tok = it.q0 + (row_valid ? r / G : 0);
-                const int64_t head = head0 + (row_valid ? r % G : 0);
-#pragma unroll 1
-                for (int c = 0; c < 2; ++c) {
-                    const int col0 = w * 64 + c * 32;
-                    uint32_t v[32];
-                    tmem_ld32(tO + col0, v);
-                    tmem_ld_wait();
-                    if (c == 1) {
-                        tc_fence_before();
-                        mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite the accumulator
+            // ---- the two partial row sums meet in the item's last-tile owner, through a ring of two slots ----
+            if (multi) {
+                if (!writer) {
+                    if (mr >= 2) {
+                        bool oke = mbar_wait(bar(B_LSEMPTY + slot), ring_par ^ 1, abort_flag, 4, -4);
+                        if (!__all_sync(0xffffffffu, oke)) { alive = false; break; }
                     }
-                    if (!row_valid) continue;
+                    xs[slot * 128 + L] = l_run;
+                    mbar_arrive(bar(B_LSFULL + slot));
+                } else {
+                    bool okf = mbar_wait(bar(B_LSFULL + slot), ring_par, abort_flag, 4, -5);
+                    if (!__all_sync(0xffffffffu, okf)) { alive = false; break; }
+                    l_run += xs[slot * 128 + L];
+                    mbar_arrive(bar(B_LSEMPTY + slot));
+                }
+            }
+            if (tid == 0) DLX_TL(3);
+            // ---- epilogue by the last tile's owner: O / l -> global ----
+            if (writer) {
+                bool ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, n);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                if (L == 0) DLX_TL(4);
+                if (warp_valid) {
+                    tc_fence_after();
+                    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
                     if (a.num_splits == 1) {
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.out) + ((tok * a.o_rs + head * HD + col0) << 1));
+                        // bf16 output, 32 head_dim columns (64 bytes of each row) per pass.  A thread holds one ROW, so
+                        // direct stores would touch 32 different lines per instruction; the pass goes through a small
+                        // swizzled staging buffer instead and leaves as 8 rows x 64 contiguous bytes per instruction.
+                        char* rowp[4];   // output rows this lane stores: warp rows 8 i + lane / 4
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            uint4 o;
-                            o.x = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 0]) * inv, __uint_as_float(v[q4 * 8 + 1]) * inv);
-                            o.y = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 2]) * inv, __uint_as_float(v[q4 * 8 + 3]) * inv);
-                            o.z = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 4]) * inv, __uint_as_float(v[q4 * 8 + 5]) * inv);
-                            o.w = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 6]) * inv, __uint_as_float(v[q4 * 8 + 7]) * inv);
-                            dst[q4] = o;
+                        for (int i = 0; i < 4; ++i) {
+                            const int R = (warp & 3) * 32 + 8 * i + (lane >> 2);
+                            const int2 dm = rowmap[R];
+                            rowp[i] = R < rows_here
+                                ? static_cast<char*>(a.out) + (((int64_t)(it.q0 + it.tok0 + dm.x) * a.o_rs + (head0 + dm.y) * HD) << 1) + (lane & 3) * 16
+                                : nullptr;
+                        }
+                        if (L == 0) DLX_TL(16);
+                        // A rolled loop on purpose: straight-line code that runs once per item is fetched from far away
+                        // every time, and a 4 x unrolled epilogue cost more in instruction fetch than it saved.
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t v[32];
+                            tmem_ld32(tO + c * 32, v);
+                            tmem_ld_wait();
+                            if (c == 3) {
+                                tc_fence_before();
+                                mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite it
+                                if (L == 0) DLX_TL(17);
+                            }
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4) {
+                                uint4 o;
+                                o.x = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 0]) * inv, __uint_as_float(v[q4 * 8 + 1]) * inv);
+                                o.y = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 2]) * inv, __uint_as_float(v[q4 * 8 + 3]) * inv);
+                                o.z = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 4]) * inv, __uint_as_float(v[q4 * 8 + 5]) * inv);
+                                o.w = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 6]) * inv, __uint_as_float(v[q4 * 8 + 7]) * inv);
+                                *reinterpret_cast<uint4*>(stage + lane * 64 + ((q4 ^ ((lane >> 1) & 3)) << 4)) = o;
+                            }
+                            __syncwarp();
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int row = 8 * i + (lane >> 2);
+                                const uint4 o = *reinterpret_cast<const uint4*>(stage + row * 64 + (((lane & 3) ^ ((row >> 1) & 3)) << 4));
+                                if (rowp[i] != nullptr) *reinterpret_cast<uint4*>(rowp[i] + c * 64) = o;
+                            }
+                            __syncwarp();
+                            if (L == 0 && c == 0) DLX_TL(18);
                         }
                     } else {
+                        const int64_t tok = it.q0 + it.tok0 + (row_valid ? my_row.x : 0);
+                        const int64_t head = head0 + (row_valid ? my_row.y : 0);
                         const int64_t e = ((int64_t)it.split * a.total_q + tok) * a.hq + head;
-                        float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + col0);
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t v[32];
+                            tmem_ld32(tO + c * 32, v);
+                            tmem_ld_wait();
+                            if (c == 3) {
+                                tc_fence_before();
+                                mbar_arrive(bar(B_OFREE));
+                            }
+                            if (!row_valid) continue;
+                            float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + c * 32);
 #pragma unroll
-                        for (int q4 = 0; q4 < 8; ++q4)
-                            dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
-                                                  __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
-                        if (c == 0 && w == 0) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
+                            for (int q4 = 0; q4 < 8; ++q4)
+                                dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
+                                                      __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
+                        }
+                        if (row_valid) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
                     }
+                } else {
+                    mbar_arrive(bar(B_OFREE));
                 }
-            } else {
-                mbar_arrive(bar(B_OFREE));
+                if (L == 0) DLX_TL(5);
             }
-            if (tid == 0) DLX_TL(5);
-            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
+            ++done; ck += n; mr += multi ? 1 : 0;
         }
     } else if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
         // =========================== loaders: one warp for K tiles, one for V tiles (and later items' Q) ==========
@@ -604,6 +710,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
         const int stages = which ? VSTAGES : KSTAGES;
         bool alive = true;
+#pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
             const Item it = get_item(round);
             if (!it.valid) continue;
@@ -627,7 +734,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 }
                 const int head0 = kvh * G;
                 int qi = (it.row0 + rbase) / G, qg = (it.row0 + rbase) % G;
-#pragma unroll 4
+#pragma unroll 1
                 for (int i = 0; i < 64; ++i) {
                     const int row = rbase + 2 * i;
                     const bool okr = row < it.rows_here;
@@ -638,14 +745,12 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 }
                 cp_async_arrive(bar(B_QFULL));
             }
+#pragma unroll 1
             for (int jj = 0; jj < n && alive; ++jj) {
                 const int idx = ck + jj;                       // running tile count: ring position
                 const int stage = idx % stages;
                 const uint32_t par_empty = ((idx / stages) & 1) ^ 1;
-                // Key tiles are taken last-to-first: the tile with the end of the cached prefix and the in-flight rows is
-                // the slow one to fetch (row-wise copies); as an item's FIRST tile its fetch overlaps the previous item's
-                // last tiles instead of sitting at the end of the item with nothing behind it to hide it.
-                const int p0 = (it.t0 + n - 1 - jj) * TILE_N;
+                const int p0 = (it.t0 + tile_of(jj, n)) * TILE_N;
                 const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
                 // A tile that holds the end of the cached prefix: its leading cached rows, in whole groups of 8 (the
                 // swizzle period), still come by TMA through the 8-row map; rows [tma_rows, c_end) go through cp.async.
@@ -657,7 +762,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     c_end = min(it.total - p0, TILE_N);
                 }
                 if (!by_tma) {
-#pragma unroll
+#pragma unroll 1
                     for (int hh = 0; hh < 4; ++hh) {
                         const int row = tma_rows + lane + 32 * hh;
                         if (row >= c_end) break;
@@ -709,7 +814,7 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                     }
                     const uint32_t dbase = d0 + half_off;
                     const int pairs = (c_end - tma_rows + 1) >> 1;
-#pragma unroll 4
+#pragma unroll 2
                     for (int i = 0; i < pairs; ++i) {
                         const int row = tma_rows + rbase + 2 * i;
                         if (row < c_end) {
@@ -726,11 +831,12 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
     } else if (warp == QK_WARP && lane == 0) {
         // =========================== Q K^T issuer (one thread) ===========================
-        // S[k & 1] = Q K(k)^T.  The first two tiles of an item start as soon as Q and K are in and the S buffers
+        // S[g & 1] = Q K(k)^T for the tile with running index g.  The first two tiles of an item start as soon as Q and K are in and the S buffers
         // are free; tile k + 2 starts when the softmax warpgroup has pulled S(k) into registers (S_free), i.e.
         // while tile k's exponentials are still running.
         constexpr uint32_t ID_QK = instr_desc(false);
         bool ok = true;
+#pragma unroll 1
         for (int round = 0; round < n_rounds && ok; ++round) {
             const Item it = get_item(round);
             if (!it.valid) continue;
@@ -743,35 +849,36 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
                 if (!ok) break;
                 DLX_TL(8);
                 mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
-                tma_load_3d(sQ, &tm_q, 0, it.kvh * G, it.q0 + it.row0 / G, bar(B_QFULL));
-                tma_load_3d(sQ + REGION, &tm_q, 64, it.kvh * G, it.q0 + it.row0 / G, bar(B_QFULL));
+                tma_load_3d(sQ, &tm_q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
+                tma_load_3d(sQ + REGION, &tm_q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
             }
             ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
             DLX_TL(9);
+#pragma unroll 1
             for (int k = 0; k < n && ok; ++k) {
-                const int u = ((k & 1) ? cb1 : cb0) + (k >> 1);   // use count of S buffer k & 1
+                const int idx = ck + k;
+                const int b = idx & 1, u = idx >> 1;   // S buffer and its use count
                 if (u >= 1) {
-                    ok = mbar_wait(bar(B_SFREE + (k & 1)), (u - 1) & 1, abort_flag, 11, k);
+                    ok = mbar_wait(bar(B_SFREE + b), (u - 1) & 1, abort_flag, 11, k);
                     if (!ok) break;
                 }
-                const int idx = ck + k;
                 ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
                 if (!ok) break;
                 fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
                 tc_fence_after();
                 const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
-                const uint32_t d = tmem + TM_S + (k & 1) * 128;
+                const uint32_t d = tmem + TM_S + b * 128;
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
                     mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
                 }
-                tc_commit(bar(B_SFULL + (k & 1)));
+                tc_commit(bar(B_SFULL + b));
                 tc_commit(bar(B_KEMPTY + idx % KSTAGES));
             }
             if (ok) tc_commit(bar(B_QEMPTY));   // every Q K^T of this item has read Q
             DLX_TL(10);
-            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
+            ++done; ck += n;
         }
     } else if (warp == PV_WARP && lane == 0) {
         // =========================== P V issuer (one thread) ===========================
@@ -780,32 +887,34 @@ decode_attn_tc5_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap t
         // and V would line up behind each other's MMAs.
         constexpr uint32_t ID_PV = instr_desc(true);
         bool ok = true;
+#pragma unroll 1
         for (int round = 0; round < n_rounds && ok; ++round) {
             const Item it = get_item(round);
             if (!it.valid) continue;
             const int n = it.n;
             if (done > 0) ok = mbar_wait(bar(B_OFREE), (done - 1) & 1, abort_flag, 8, -2);  // the epilogue has read O
             DLX_TL(11);
+#pragma unroll 1
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
-                const int u = ((k & 1) ? cb1 : cb0) + (k >> 1);
+                const int b = idx & 1, u = idx >> 1;   // P buffer and its use count
                 ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k) &&
-                     mbar_wait(bar(B_PFULL + (k & 1)), u & 1, abort_flag, 9, k);
+                     mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                 if (!ok) break;
                 if (k == 0) DLX_TL(12);
                 fence_async_proxy();
                 tc_fence_after();
                 const uint32_t vb = sV + (idx % VSTAGES) * ITEM_BYTES;
-                const uint32_t pa = tmem + TM_P + (k & 1) * 64;
+                const uint32_t pa = tmem + TM_P + b * 64;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(bar(B_PFREE + (k & 1)));
+                tc_commit(bar(B_PFREE + b));
                 tc_commit(bar(B_VEMPTY + idx % VSTAGES));
             }
             if (ok) tc_commit(bar(B_OFULL));
             DLX_TL(13);
-            ++done; ck += n; cb0 += (n + 1) >> 1; cb1 += n >> 1;
+            ++done; ck += n;
         }
     }
 
@@ -953,8 +1062,8 @@ int read_tc5_status(int out[4]) {
 
 #if DLX_TC5_PROFILE
 extern "C" int dlx_debug_timeline(unsigned long long* out) {   // profile build only: copies out and clears [8][16] event times
-    cudaError_t e = cudaMemcpyFromSymbol(out, tc5::g_tl, sizeof(unsigned long long) * 128);
-    unsigned long long zero[128] = {};
+    cudaError_t e = cudaMemcpyFromSymbol(out, tc5::g_tl, sizeof(unsigned long long) * 192);
+    unsigned long long zero[192] = {};
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_tl, zero, sizeof(zero));
     return e == cudaSuccess ? DLX_OK : DLX_ERR_CUDA;
 }
