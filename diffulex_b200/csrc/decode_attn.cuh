@@ -20,6 +20,7 @@ struct DecodeArgs {
     int mask_mode, dbs;
     int num_splits, m_blocks;
     int tma_box_rows;  // tcgen05 kernel: rows per TMA box (0 = cached tiles are not fetched by TMA)
+    int tma_lvl0;      // tcgen05 kernel: level of the largest usable box (rows = 128 >> level)
     int q_tokens;      // tcgen05 kernel: whole tokens per 128-row block (128 / group)
     int q_by_tma;      // tcgen05 kernel: Q blocks are fetched by TMA (else by 16-byte cp.async)
     int items_total;   // tcgen05 kernel: num_seqs * hkv * m_blocks * num_splits work items, walked by persistent CTAs

@@ -54,11 +54,11 @@ constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
-constexpr int BT_SLOTS = 1024;                     // 4 KiB each: 262 k tokens at 256-token pages
-constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 4 x 128 floats: two slots of row references, two of partial row sums
-constexpr int OFF_STAGE = OFF_XCH + 4 * 128 * 4;   // output staging: 32 rows x 64 bytes per softmax warp
-constexpr int STAGE_WARP_BYTES = 32 * 64;
-constexpr int OFF_ROWMAP = OFF_STAGE + 8 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group) of a block's rows
+constexpr int BT_SLOTS = 512;                      // 2 KiB each: 131 k tokens at 256-token pages
+constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 8 x 128 floats: two slots of row references; two slots of (row sums x 2, reference)
+constexpr int OFF_STAGE = OFF_XCH + 8 * 128 * 4;   // output staging: 32 rows x 128 bytes per epilogue warp
+constexpr int STAGE_WARP_BYTES = 32 * 128;
+constexpr int OFF_ROWMAP = OFF_STAGE + 4 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group) of a block's rows
 constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;   // this CTA's decoded work items, one per round
 constexpr int MAX_ROUNDS = 64;                     // more rounds than this: every role decodes its items itself
 constexpr int ITEM_SLOT = 64;                      // bytes per decoded item
@@ -71,7 +71,17 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 // RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
 // device status word is set.  Earlier keys then weigh < 2^-100 of the result, far below fp32 resolution.
 #define RAISE_LIMIT 100.f
-constexpr int NUM_THREADS = 384;
+constexpr int NUM_THREADS = 512;
+// Registers per thread after the roles split (the kernel starts with 65536 / 512 = 128 each): the four helper warps
+// and the epilogue warpgroup give registers back, the two softmax warpgroups (a row of 128 scores each) take them.
+#ifndef DLX_SOFTMAX_REGS
+#define DLX_SOFTMAX_REGS 176
+#define DLX_HELPER_REGS 64
+#define DLX_EPI_REGS 96
+#endif
+constexpr int SOFTMAX_REGS = DLX_SOFTMAX_REGS, HELPER_REGS = DLX_HELPER_REGS, EPI_REGS = DLX_EPI_REGS;
+static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget");
+constexpr int EPI_WARP0 = 12;
 constexpr int KLOAD_WARP = 8, VLOAD_WARP = 9, QK_WARP = 10, PV_WARP = 11;
 constexpr int NUM_LOADERS = 32;                    // lanes of one loader warp
 constexpr uint32_t WAIT_LIMIT = 1u << 21;
@@ -92,8 +102,8 @@ enum {
     // Rings of two slots between the warpgroups, one use per item with two or more tiles:
     B_MRFULL = 22,  // [slot] the row references of the item's first tile are in shared memory
     B_MREMPTY = 24, // [slot] ... and have been read by the owner of the item's second tile
-    B_LSFULL = 26,  // [slot] the partial row sums of the warpgroup that does not write the item's output are in
-    B_LSEMPTY = 28, // [slot] ... and have been added by the one that does
+    B_LSFULL = 26,  // [slot] both warpgroups' partial row sums of an item are in shared memory (one use per item)
+    B_LSEMPTY = 28, // [slot] ... and the epilogue warpgroup has read them
     B_COUNT = 30
 };
 
@@ -125,26 +135,23 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
 }
-// Slow half of a bounded wait, out of line (there are ~40 wait sites): keeps polling up to the limit, gives up early when
-// another thread of the CTA has, and on expiry raises the CTA's abort flag and records (site, tile, CTA).
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
+// Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.  Kept tiny, because it
+// is inlined at some forty sites (a called function cannot be used once the warps have resized their register
+// files): on expiry the site and tile go into the CTA's abort word, which one thread copies to the device status
+// word when the CTA retires.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
+    if (mbar_try(bar, parity)) return true;
+#pragma unroll 1
     for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
         if (mbar_try(bar, parity)) return true;
         if ((it & 255u) == 255u && *abort_flag) return false;
     }
-    *abort_flag = 1;
-    if (atomicCAS(&g_status[0], 0, 1) == 0) {
-        g_status[1] = role; g_status[2] = tile;
-        g_status[3] = blockIdx.x;
-    }
+    *abort_flag = 1 | ((tile & 0xffff) << 8) | (role << 24);
     return false;
 }
-// Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
-    if (mbar_try(bar, parity)) return true;
-    return mbar_wait_slow(bar, parity, abort_flag, role, tile);
-}
 
+template <int N> __device__ __forceinline__ void reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
+template <int N> __device__ __forceinline__ void reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_async_proxy() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -249,8 +256,7 @@ struct alignas(8) Item {
     int t0, n;
 };
 
-// Not inlined: five call sites, ~3 KB of code each, and instruction-cache room is what the per-item code paths lack.
-__device__ __noinline__ Item load_item(const DecodeArgs& a, int item) {
+__device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
     Item it;
     it.valid = false; it.empty_split = false;
     it.seq = it.kvh = it.split = 0;
@@ -308,10 +314,17 @@ __device__ __forceinline__ int tile_of(int jj, int n) { return n - 1 - ((jj < 2 
 // Every role keeps running counters for the rings and buffers, so the pipeline never drains between items:
 // while the softmax warpgroups finish item i the loaders already fetch Q / K / V of item i + 1 and the Q K^T
 // issuer fills its first two S buffers.
+// Tensor maps of one launch: the K and V caches as {head_dim, Hkv, page row, page} with boxes of 128 >> level rows
+// (level 0..4: 128, 64, 32, 16, 8 rows; levels whose box would exceed a page are unused), and Q.
+struct TmaMaps {
+    CUtensorMap k[5], v[5], q;
+};
+
+// TABLE: the CTA's rounds fit the shared-memory item table (the usual case); otherwise every role decodes its items
+// itself, at the price of five inlined copies of the decoder, which is why that is a separate instantiation.
+template <bool TABLE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k8,
-                       const __grid_constant__ CUtensorMap tm_v8) {
+decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps maps) {
     extern __shared__ unsigned char smem_raw[];
 #if DLX_TC5_PROFILE
     const long long t_entry = clock64();
@@ -358,7 +371,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
         mbar_init(bar(B_OFREE), 128);
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(B_MRFULL + s), 128); mbar_init(bar(B_MREMPTY + s), 128);
-            mbar_init(bar(B_LSFULL + s), 128); mbar_init(bar(B_LSEMPTY + s), 128);
+            mbar_init(bar(B_LSFULL + s), 256); mbar_init(bar(B_LSEMPTY + s), 128);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -375,13 +388,15 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
     // All rounds are decoded up front, one thread per round: the chain of dependent metadata loads (sequence order ->
     // lengths -> offsets, ~2 us) is paid once per CTA instead of once per item and role.
     Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
-    const bool items_in_smem = n_rounds <= MAX_ROUNDS;
-    if (items_in_smem && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
+    if (TABLE && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
     int2* rowmap = reinterpret_cast<int2*>(gbase + OFF_ROWMAP);
     if (tid >= 128 && tid < 256) rowmap[tid - 128] = make_int2((tid - 128) / G, (tid - 128) % G);
-    auto get_item = [&](int k) { return items_in_smem ? items_s[k] : load_item(a, item_of_round(k)); };
+    auto get_item = [&](int k) {
+        if constexpr (TABLE) return items_s[k];
+        else return load_item(a, item_of_round(k));
+    };
     {
         // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
         // by a Q box: zero them once, so that the unused TMEM lanes only ever see finite scores.
@@ -412,6 +427,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
     int done = 0, ck = 0;
 
     if (warp < 8) {
+        reg_inc<SOFTMAX_REGS>();
         // =========================== softmax warpgroups ===========================
         // Two warpgroups own the same 128 rows (thread = row = TMEM lane) and take alternate key tiles, counted ACROSS
         // items: the tile with running index g belongs to warpgroup g & 1, which always works on S buffer / P buffer
@@ -419,15 +435,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
         // while one waits for its S the other works.  Both scale their P by the SAME per-row reference m_ref = scaled
         // row maximum of the item's first tile (a fixed reference is exact as long as exponents stay in range: see
         // RAISE_LIMIT), so their outputs add up in the one O accumulator and their row sums add up at the end.
-        // The warpgroup that owns an item's last tile writes the item's output; the other one is by then already
-        // working on the next item's first tile, whose S is waiting in TMEM.
+        // Neither waits for an item's output to be written: that is the epilogue warpgroup's job.
         const int w = warp >> 2;                       // warpgroup = parity of the running tile index
         const int L = tid & 127;                       // TMEM lane == row inside the tile
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64, tO = lane_base + TM_O;
+        const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64;
         float* xm = reinterpret_cast<float*>(gbase + OFF_XCH);    // [2][128] row references, ring of two items
-        float* xs = xm + 256;                                     // [2][128] partial row sums, ring of two items
-        unsigned char* stage = gbase + OFF_STAGE + warp * STAGE_WARP_BYTES;   // output staging of this warp
+        float* xs = xm + 256;                                     // [2][3][128] per item: row sums of each warpgroup, reference
         const float sl2 = a.scale_log2;
         int mr = 0;                                    // items with two or more tiles so far: position in both rings
         bool alive = true;
@@ -450,7 +464,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
             const bool warp_valid = (warp & 3) * 32 < rows_here;  // any valid row in this warp?
             const bool row_valid = L < rows_here;
             const int jj_first = (w ^ ck) & 1;             // this warpgroup's first tile of the item (0 or 1)
-            const bool writer = ((ck + n - 1) & 1) == w;   // owns the last tile: runs the epilogue
             const bool multi = n >= 2;                     // both warpgroups have tiles: reference and sums are exchanged
             const int slot = mr & 1;
             const uint32_t ring_par = (mr >> 1) & 1;
@@ -580,118 +593,126 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
                         if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
                     }
                 }
-                if (jj == n - 1 && done >= 1) {
-                    // This warpgroup will wait for the item's O_full next.  It may not have watched the previous item's
-                    // (the other warpgroup wrote that one), and a parity wait can only tell the current phase from the
-                    // one before: make sure the previous phase is over while this item's cannot complete yet.
-                    bool oko = mbar_wait(bar(B_OFULL), (done - 1) & 1, abort_flag, 3, -6);
-                    if (!__all_sync(0xffffffffu, oko)) { alive = false; break; }
-                }
                 tc_fence_before();
                 mbar_arrive(bar(B_PFULL + w));
             }
             if (L == 0) DLX_TL(w ? 7 : 2);
             if (!alive) break;
-            // ---- the two partial row sums meet in the item's last-tile owner, through a ring of two slots ----
-            if (multi) {
-                if (!writer) {
-                    if (mr >= 2) {
-                        bool oke = mbar_wait(bar(B_LSEMPTY + slot), ring_par ^ 1, abort_flag, 4, -4);
-                        if (!__all_sync(0xffffffffu, oke)) { alive = false; break; }
-                    }
-                    xs[slot * 128 + L] = l_run;
-                    mbar_arrive(bar(B_LSFULL + slot));
-                } else {
-                    bool okf = mbar_wait(bar(B_LSFULL + slot), ring_par, abort_flag, 4, -5);
-                    if (!__all_sync(0xffffffffu, okf)) { alive = false; break; }
-                    l_run += xs[slot * 128 + L];
-                    mbar_arrive(bar(B_LSEMPTY + slot));
+            // ---- hand the item over to the epilogue warpgroup: partial row sums (and the reference) through a ring of
+            // two slots, one use per item.  A warpgroup without a tile in the item (one-tile items) hands over a zero.
+            {
+                const int ls = done & 1;
+                if (done >= 2) {
+                    bool oke = mbar_wait(bar(B_LSEMPTY + ls), ((done >> 1) & 1) ^ 1, abort_flag, 4, -4);
+                    if (!__all_sync(0xffffffffu, oke)) { alive = false; break; }
                 }
+                xs[ls * 384 + w * 128 + L] = l_run;
+                if (jj_first == 0) xs[ls * 384 + 256 + L] = m_ref;   // the owner of tile 0 set it
+                mbar_arrive(bar(B_LSFULL + ls));
             }
             if (tid == 0) DLX_TL(3);
-            // ---- epilogue by the last tile's owner: O / l -> global ----
-            if (writer) {
-                bool ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, n);
-                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                if (L == 0) DLX_TL(4);
-                if (warp_valid) {
-                    tc_fence_after();
-                    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-                    if (a.num_splits == 1) {
-                        // bf16 output, 32 head_dim columns (64 bytes of each row) per pass.  A thread holds one ROW, so
-                        // direct stores would touch 32 different lines per instruction; the pass goes through a small
-                        // swizzled staging buffer instead and leaves as 8 rows x 64 contiguous bytes per instruction.
-                        char* rowp[4];   // output rows this lane stores: warp rows 8 i + lane / 4
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int R = (warp & 3) * 32 + 8 * i + (lane >> 2);
-                            const int2 dm = rowmap[R];
-                            rowp[i] = R < rows_here
-                                ? static_cast<char*>(a.out) + (((int64_t)(it.q0 + it.tok0 + dm.x) * a.o_rs + (head0 + dm.y) * HD) << 1) + (lane & 3) * 16
-                                : nullptr;
-                        }
-                        if (L == 0) DLX_TL(16);
-                        // A rolled loop on purpose: straight-line code that runs once per item is fetched from far away
-                        // every time, and a 4 x unrolled epilogue cost more in instruction fetch than it saved.
-#pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t v[32];
-                            tmem_ld32(tO + c * 32, v);
-                            tmem_ld_wait();
-                            if (c == 3) {
-                                tc_fence_before();
-                                mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite it
-                                if (L == 0) DLX_TL(17);
-                            }
-#pragma unroll
-                            for (int q4 = 0; q4 < 4; ++q4) {
-                                uint4 o;
-                                o.x = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 0]) * inv, __uint_as_float(v[q4 * 8 + 1]) * inv);
-                                o.y = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 2]) * inv, __uint_as_float(v[q4 * 8 + 3]) * inv);
-                                o.z = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 4]) * inv, __uint_as_float(v[q4 * 8 + 5]) * inv);
-                                o.w = pack2<__nv_bfloat16>(__uint_as_float(v[q4 * 8 + 6]) * inv, __uint_as_float(v[q4 * 8 + 7]) * inv);
-                                *reinterpret_cast<uint4*>(stage + lane * 64 + ((q4 ^ ((lane >> 1) & 3)) << 4)) = o;
-                            }
-                            __syncwarp();
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const int row = 8 * i + (lane >> 2);
-                                const uint4 o = *reinterpret_cast<const uint4*>(stage + row * 64 + (((lane & 3) ^ ((row >> 1) & 3)) << 4));
-                                if (rowp[i] != nullptr) *reinterpret_cast<uint4*>(rowp[i] + c * 64) = o;
-                            }
-                            __syncwarp();
-                            if (L == 0 && c == 0) DLX_TL(18);
-                        }
-                    } else {
-                        const int64_t tok = it.q0 + it.tok0 + (row_valid ? my_row.x : 0);
-                        const int64_t head = head0 + (row_valid ? my_row.y : 0);
-                        const int64_t e = ((int64_t)it.split * a.total_q + tok) * a.hq + head;
-#pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t v[32];
-                            tmem_ld32(tO + c * 32, v);
-                            tmem_ld_wait();
-                            if (c == 3) {
-                                tc_fence_before();
-                                mbar_arrive(bar(B_OFREE));
-                            }
-                            if (!row_valid) continue;
-                            float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + c * 32);
-#pragma unroll
-                            for (int q4 = 0; q4 < 8; ++q4)
-                                dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
-                                                      __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
-                        }
-                        if (row_valid) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
-                    }
-                } else {
-                    mbar_arrive(bar(B_OFREE));
-                }
-                if (L == 0) DLX_TL(5);
-            }
             ++done; ck += n; mr += multi ? 1 : 0;
         }
-    } else if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
+    } else if (warp >= EPI_WARP0) {
+        // =========================== epilogue warpgroup: O / l -> global ===========================
+        // Its own four warps (TMEM lanes 32 (warp % 4) ..), so that the softmax warpgroups go from an item's last
+        // tile straight to the next item's first: the output of item i is written while item i + 1 is computed.
+        reg_dec<EPI_REGS>();
+        const int L = tid & 127, wq = warp & 3;
+        const uint32_t tO = tmem + ((uint32_t)(wq * 32) << 16) + TM_O;
+        const float* xs = reinterpret_cast<const float*>(gbase + OFF_XCH) + 256;
+        unsigned char* stage = gbase + OFF_STAGE + wq * STAGE_WARP_BYTES;   // 32 rows x 128 bytes of this warp
+        bool alive = true;
+#pragma unroll 1
+        for (int round = 0; round < n_rounds && alive; ++round) {
+            const Item it = get_item(round);
+            if (!it.valid) continue;
+            const int ls = done & 1;
+            bool ok = mbar_wait(bar(B_LSFULL + ls), (done >> 1) & 1, abort_flag, 12, -5);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const float l_run = xs[ls * 384 + L] + xs[ls * 384 + 128 + L];
+            const float m_ref = xs[ls * 384 + 256 + L];
+            mbar_arrive(bar(B_LSEMPTY + ls));
+            ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, it.n);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            if (L == 0) DLX_TL(4);
+            tc_fence_after();
+            const int rows_here = it.rows_here;
+            const int head0 = it.kvh * G;
+            const bool row_valid = L < rows_here;
+            if (wq * 32 < rows_here) {
+                const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+                if (a.num_splits == 1) {
+                    // bf16 output, 64 head_dim columns (128 bytes of each row) per pass.  A thread holds one ROW, so direct
+                    // stores would touch 32 different lines per instruction; the pass goes through a swizzled staging
+                    // buffer instead and leaves as 4 rows x 128 contiguous bytes per instruction.
+#pragma unroll 1
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t v[2][32];
+                        tmem_ld32(tO + c * 64, v[0]);
+                        tmem_ld32(tO + c * 64 + 32, v[1]);
+                        tmem_ld_wait();
+                        if (c == 1) {
+                            tc_fence_before();
+                            mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite it
+                            if (L == 0) DLX_TL(17);
+                        }
+#pragma unroll
+                        for (int q4 = 0; q4 < 8; ++q4) {
+                            const uint32_t* x = &v[q4 >> 2][(q4 & 3) * 8];
+                            uint4 o;
+                            o.x = pack2<__nv_bfloat16>(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv);
+                            o.y = pack2<__nv_bfloat16>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv);
+                            o.z = pack2<__nv_bfloat16>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv);
+                            o.w = pack2<__nv_bfloat16>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv);
+                            *reinterpret_cast<uint4*>(stage + lane * 128 + ((q4 ^ (lane & 7)) << 4)) = o;
+                        }
+                        __syncwarp();
+#pragma unroll 2
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = 4 * i + (lane >> 3);
+                            const int R = wq * 32 + row;
+                            const uint4 o = *reinterpret_cast<const uint4*>(stage + row * 128 + (((lane & 7) ^ (row & 7)) << 4));
+                            if (R < rows_here) {
+                                const int2 dm = rowmap[R];
+                                char* dst = static_cast<char*>(a.out) + (((int64_t)(it.q0 + it.tok0 + dm.x) * a.o_rs + (int64_t)(head0 + dm.y) * HD) << 1);
+                                *reinterpret_cast<uint4*>(dst + c * 128 + (lane & 7) * 16) = o;
+                            }
+                        }
+                        __syncwarp();
+                    }
+                } else {
+                    const int2 my_row = rowmap[L];
+                    const int64_t tok = it.q0 + it.tok0 + (row_valid ? my_row.x : 0);
+                    const int64_t head = head0 + (row_valid ? my_row.y : 0);
+                    const int64_t e = ((int64_t)it.split * a.total_q + tok) * a.hq + head;
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t v[32];
+                        tmem_ld32(tO + c * 32, v);
+                        tmem_ld_wait();
+                        if (c == 3) {
+                            tc_fence_before();
+                            mbar_arrive(bar(B_OFREE));
+                        }
+                        if (!row_valid) continue;
+                        float4* dst = reinterpret_cast<float4*>(a.ws_o + e * HD + c * 32);
+#pragma unroll
+                        for (int q4 = 0; q4 < 8; ++q4)
+                            dst[q4] = make_float4(__uint_as_float(v[q4 * 4 + 0]) * inv, __uint_as_float(v[q4 * 4 + 1]) * inv,
+                                                  __uint_as_float(v[q4 * 4 + 2]) * inv, __uint_as_float(v[q4 * 4 + 3]) * inv);
+                    }
+                    if (row_valid) a.ws_lse[e] = l_run > 0.f ? m_ref + log2f(l_run) : -INFINITY;
+                }
+            } else {
+                mbar_arrive(bar(B_OFREE));
+            }
+            if (L == 0) DLX_TL(5);
+            ++done;
+        }
+    } else {
+    reg_dec<HELPER_REGS>();   // one site for the whole helper warpgroup (warps 8..11)
+    if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
         // =========================== loaders: one warp for K tiles, one for V tiles (and later items' Q) ==========
         // Separate warps so that K (needed two tiles ahead by Q K^T) never queues behind a V tile that is still
         // waiting for its ring slot.  The rings run across items: while the softmax works on the tail of one item,
@@ -751,17 +772,25 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
                 const int stage = idx % stages;
                 const uint32_t par_empty = ((idx / stages) & 1) ^ 1;
                 const int p0 = (it.t0 + tile_of(jj, n)) * TILE_N;
-                const bool by_tma = a.tma_box_rows > 0 && p0 + TILE_N <= ctx;
+                const bool tma_on = a.tma_box_rows > 0;
+                const bool by_tma = tma_on && p0 + TILE_N <= ctx;
                 // A tile that holds the end of the cached prefix: its leading cached rows, in whole groups of 8 (the
-                // swizzle period), still come by TMA through the 8-row map; rows [tma_rows, c_end) go through cp.async.
-                // With TMA on, rows past the last key are not written at all: they keep what an earlier tile (or the
-                // zero fill at kernel start) left there, which is finite, and their scores are masked to -inf.
+                // swizzle period), still come by TMA, as boxes of 64, 32, 16 and 8 rows; rows [tma_rows, c_end) go
+                // through cp.async.  With TMA on, rows past the last key are not written at all: they keep what an
+                // earlier tile (or the zero fill at kernel start) left there, which is finite, and their scores are
+                // masked to -inf.
                 int tma_rows = 0, c_end = TILE_N;
-                if (!by_tma && a.tma_box_rows > 0) {
+                if (!by_tma && tma_on) {
                     tma_rows = max(min(ctx - p0, TILE_N), 0) & ~7;
                     c_end = min(it.total - p0, TILE_N);
                 }
+                // With TMA on, pages are walked incrementally from the tile's first (page, row): one division per tile.
+                int pj = 0, prow = 0;
+                if (tma_on) { pj = p0 / a.page_size; prow = p0 - pj * a.page_size; }
                 if (!by_tma) {
+                    int pj2 = pj, prow2 = prow + tma_rows;   // page and row of key p0 + tma_rows
+                    if (tma_on && prow2 >= a.page_size) { pj2 += prow2 / a.page_size; prow2 %= a.page_size; }
+                    const int64_t pid2 = (tma_on && pj2 < a.max_blocks) ? (int64_t)bt[pj2] : -1;
 #pragma unroll 1
                     for (int hh = 0; hh < 4; ++hh) {
                         const int row = tma_rows + lane + 32 * hh;
@@ -769,10 +798,15 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
                         const int p = p0 + row;
                         const char* ptr = nullptr;
                         if (p < ctx) {
-                            const int j = p / a.page_size;
-                            const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
-                            if (pid >= 0 && pid < a.num_pages)
-                                ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
+                            if (tma_on) {   // the cached rows left over after the boxes: fewer than 8, all in one page
+                                if (pid2 >= 0 && pid2 < a.num_pages)
+                                    ptr = cache + ((pid2 * a.page_stride + (int64_t)(prow2 + row - tma_rows) * a.token_stride + kvh * HD) << 1);
+                            } else {
+                                const int j = p / a.page_size;
+                                const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
+                                if (pid >= 0 && pid < a.num_pages)
+                                    ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
+                            }
                         } else if (p < it.total) {
                             ptr = fresh + (((int64_t)(it.kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
                         }
@@ -785,33 +819,29 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
                 const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
                 const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
                 if (jj == 0 && lane == 0) DLX_TL(14 + which);
-                if (by_tma) {
+                const CUtensorMap* lvl_maps = which ? maps.v : maps.k;
+                if (by_tma || tma_rows > 0) {
                     if (lane == 0) {
-                        mbar_arrive_expect_tx(full, ITEM_BYTES);
-                        const CUtensorMap* map = which ? &tm_v : &tm_k;
-                        const int rows = a.tma_box_rows;               // min(128, page_size)
-                        for (int r0 = 0; r0 < TILE_N; r0 += rows) {    // one box pair per page touched
-                            const int j = (p0 + r0) / a.page_size;
-                            const int pid = j < a.max_blocks ? bt[j] : -1;   // a bad id is out of bounds: zero fill
-                            const int rin = (p0 + r0) - j * a.page_size;
-                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
-                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
+                        const int rows_by_tma = by_tma ? TILE_N : tma_rows;
+                        if (by_tma) mbar_arrive_expect_tx(full, ITEM_BYTES);
+                        else mbar_expect_tx(full, (uint32_t)tma_rows * 256u);
+                        int r0 = 0;
+                        int lvl = a.tma_lvl0;                        // largest usable box: min(128, page_size) rows
+#pragma unroll 1
+                        for (int sz = TILE_N >> lvl; sz >= 8; sz >>= 1, ++lvl) {
+                            while (rows_by_tma - r0 >= sz) {         // more than once only at the largest size
+                                const int pid = pj < a.max_blocks ? bt[pj] : -1;   // a bad id is out of bounds: zero fill
+                                tma_load_4d(d0 + r0 * 128, &lvl_maps[lvl], 0, kvh, prow, pid, full);
+                                tma_load_4d(d0 + REGION + r0 * 128, &lvl_maps[lvl], 64, kvh, prow, pid, full);
+                                r0 += sz; prow += sz;
+                                if (prow >= a.page_size) { prow = 0; ++pj; }   // boxes never straddle a page
+                            }
                         }
-                    } else {
+                    } else if (by_tma) {
                         mbar_arrive(full);
                     }
-                } else {
-                    if (tma_rows > 0 && lane == 0) {
-                        mbar_expect_tx(full, (uint32_t)tma_rows * 256u);
-                        const CUtensorMap* map = which ? &tm_v8 : &tm_k8;
-                        for (int r0 = 0; r0 < tma_rows; r0 += 8) {
-                            const int j = (p0 + r0) / a.page_size;
-                            const int pid = j < a.max_blocks ? bt[j] : -1;
-                            const int rin = (p0 + r0) - j * a.page_size;
-                            tma_load_4d(d0 + r0 * 128, map, 0, kvh, rin, pid, full);
-                            tma_load_4d(d0 + REGION + r0 * 128, map, 64, kvh, rin, pid, full);
-                        }
-                    }
+                }
+                if (!by_tma) {
                     const uint32_t dbase = d0 + half_off;
                     const int pairs = (c_end - tma_rows + 1) >> 1;
 #pragma unroll 2
@@ -829,7 +859,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
             ++done; ck += n;
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
-    } else if (warp == QK_WARP && lane == 0) {
+    } else if (warp == QK_WARP) {
+      if (lane == 0) {
         // =========================== Q K^T issuer (one thread) ===========================
         // S[g & 1] = Q K(k)^T for the tile with running index g.  The first two tiles of an item start as soon as Q and K are in and the S buffers
         // are free; tile k + 2 starts when the softmax warpgroup has pulled S(k) into registers (S_free), i.e.
@@ -849,8 +880,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
                 if (!ok) break;
                 DLX_TL(8);
                 mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
-                tma_load_3d(sQ, &tm_q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
-                tma_load_3d(sQ + REGION, &tm_q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
+                tma_load_3d(sQ, &maps.q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
+                tma_load_3d(sQ + REGION, &maps.q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
             }
             ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
             DLX_TL(9);
@@ -880,7 +911,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
             DLX_TL(10);
             ++done; ck += n;
         }
-    } else if (warp == PV_WARP && lane == 0) {
+      }
+    } else if (warp == PV_WARP) {
+      if (lane == 0) {
         // =========================== P V issuer (one thread) ===========================
         // O += P(k) V(k), in tile order (one thread, so the accumulation order is fixed).  A second issuing
         // thread, because tcgen05.mma issue blocks while the pipe is busy: with one thread the waits for P, K
@@ -916,11 +949,19 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ CUtenso
             DLX_TL(13);
             ++done; ck += n;
         }
+      }
     }
-
+    }
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
+    if (tid == 0 && *abort_flag != 0) {   // a wait ran out: record where (the first CTA to report wins)
+        const int word = *abort_flag;
+        if (atomicCAS(&g_status[0], 0, 1) == 0) {
+            g_status[1] = (word >> 24) & 0xff; g_status[2] = (int)(short)((word >> 8) & 0xffff);
+            g_status[3] = blockIdx.x;
+        }
+    }
     if (warp == QK_WARP) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem) : "memory");
@@ -994,44 +1035,44 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 16 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              tc5::SMEM_BYTES);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc5::SMEM_BYTES);
         if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "cudaFuncSetAttribute(tc5 smem=%d): %s", tc5::SMEM_BYTES, cudaGetErrorString(e));
         attr_done[dev] = true;
     }
     DecodeArgs a = a_in;
-    CUtensorMap tm_k, tm_v, tm_q, tm_k8, tm_v8;
-    memset(&tm_k8, 0, sizeof(tm_k8));
-    memset(&tm_v8, 0, sizeof(tm_v8));
-    memset(&tm_k, 0, sizeof(tm_k));
-    memset(&tm_v, 0, sizeof(tm_v));
-    memset(&tm_q, 0, sizeof(tm_q));
+    tc5::TmaMaps maps;
+    memset(&maps, 0, sizeof(maps));
     // TMA serves tiles of 128 cached keys when a tile is a whole number of equal boxes: the page size is a
     // multiple of 128 rows, or divides 128 and is a multiple of the 8-row swizzle period.
     a.tma_box_rows = 0;
+    a.tma_lvl0 = 0;
     const int ps = a.page_size;
     const bool fits = a.max_blocks > 0 && a.num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
     const bool strides_ok = a.token_stride * 2 % 16 == 0 && a.page_stride * 2 % 16 == 0 &&
                             a.page_stride * 2 < (1ll << 40) && a.num_pages < (1ll << 31);
     if (fits && strides_ok && getenv("DLX_TC5_NO_TMA") == nullptr) {
         const int rows = ps < 128 ? ps : 128;
-        MapKey kk{a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
-        MapKey kv{a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows};
-        MapKey kk8 = kk, kv8 = kv;   // 8-row boxes for the tile that holds the end of the cached prefix
-        kk8.rows = kv8.rows = 8;
-        int rc = cache_map(kk, &tm_k);
-        if (rc == DLX_OK) rc = cache_map(kv, &tm_v);
-        if (rc == DLX_OK) rc = cache_map(kk8, &tm_k8);
-        if (rc == DLX_OK) rc = cache_map(kv8, &tm_v8);
-        if (rc != DLX_OK) return rc;
+        int lvl0 = 0;
+        while ((128 >> lvl0) > rows) ++lvl0;
+        for (int lvl = lvl0; lvl < 5; ++lvl) {   // boxes of 128 >> lvl rows: whole tiles use lvl0, tail tiles all of them
+            MapKey kk{a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 128 >> lvl};
+            MapKey kv{a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 128 >> lvl};
+            int rc = cache_map(kk, &maps.k[lvl]);
+            if (rc == DLX_OK) rc = cache_map(kv, &maps.v[lvl]);
+            if (rc != DLX_OK) return rc;
+        }
         a.tma_box_rows = rows;
+        a.tma_lvl0 = lvl0;
     }
     // Q blocks of 128 / group whole tokens: one box {64, group, tokens} per head_dim half
     a.q_tokens = 128 / a.group;
     a.q_by_tma = 0;
     if (a.total_q > 0 && a.q_rs * 2 % 16 == 0 && a.q_rs * 2 < (1ll << 40) && getenv("DLX_TC5_NO_TMA") == nullptr) {
         MapKey kq{a.q, a.q_rs, 0, a.total_q, a.hq, a.group, a.q_tokens, 3};
-        const int rc = cache_map(kq, &tm_q);
+        const int rc = cache_map(kq, &maps.q);
         if (rc != DLX_OK) return rc;
         a.q_by_tma = 1;
     }
@@ -1047,7 +1088,11 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     a.items_total = (int)items;
     if (const char* g = getenv("DLX_TC5_GRID")) sms = atoi(g) > 0 ? atoi(g) : sms;
     dim3 grid((unsigned)(items < sms ? items : sms)), block(tc5::NUM_THREADS);
-    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, tm_k, tm_v, tm_q, tm_k8, tm_v8);
+    const int64_t rounds = (items + grid.x - 1) / grid.x;
+    if (rounds <= tc5::MAX_ROUNDS && rounds <= tc5::NUM_THREADS)
+        tc5::decode_attn_tc5_kernel<true><<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
+    else
+        tc5::decode_attn_tc5_kernel<false><<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
     return check_launch("decode_attn_tc5_kernel");
 }
 
