@@ -48,11 +48,15 @@ constexpr int TILE_N = 128;               // keys per K/V tile
 constexpr int REGION = 128 * 128;         // [128 rows][64 bf16] 128B-swizzled block: 16 KiB
 constexpr int Q_BYTES = 2 * REGION;       // one Q tile, 2 head_dim halves
 constexpr int ITEM_BYTES = 2 * REGION;    // one K tile or one V tile
-constexpr int KSTAGES = 3, VSTAGES = 2;   // Q K^T runs two tiles ahead of P V, so K needs one stage more
+#ifndef DLX_KSTAGES
+#define DLX_KSTAGES 2
+#define DLX_VSTAGES 3
+#endif
+constexpr int KSTAGES = DLX_KSTAGES, VSTAGES = DLX_VSTAGES;   // Q K^T runs two tiles ahead of P V, so K needs one stage more
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
-constexpr int OFF_TAB = OFF_BAR + 256;             // row-source pointer tables: one per loader warp, 128 rows
+constexpr int OFF_TAB = OFF_BAR + 512;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
 constexpr int BT_SLOTS = 512;                      // 2 KiB each: 131 k tokens at 256-token pages
 constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 8 x 128 floats: two slots of row references; two slots of (row sums x 2, reference)
@@ -90,21 +94,21 @@ constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
 
 // barrier slots (8 bytes each) at OFF_BAR
 enum {
-    B_QFULL = 0, B_KFULL = 1, B_VFULL = 4, B_KEMPTY = 6, B_VEMPTY = 9,
-    B_SFULL = 11,   // [S buffer]
-    B_PFULL = 13,   // [P buffer]: the softmax may be two tiles ahead of the P V that consumes its output and an
+    B_QFULL = 0, B_KFULL = 1, B_VFULL = 4, B_KEMPTY = 7, B_VEMPTY = 10,   // K and V: up to 3 stages each
+    B_SFULL = 13,   // [S buffer]
+    B_PFULL = 15,   // [P buffer]: the softmax may be two tiles ahead of the P V that consumes its output and an
                     // mbarrier can only be one phase ahead of its waiter, hence one barrier per buffer
-    B_OFULL = 15,
-    B_OFREE = 16,   // the epilogue has O in registers: the next item's P V may overwrite the accumulator
-    B_QEMPTY = 17,  // every Q K^T of the item has run: the next item's Q may be loaded
-    B_SFREE = 18,   // [S buffer]: its scores are in the softmax warpgroup's registers, Q K^T may overwrite it
-    B_PFREE = 20,   // [P buffer]: the P V that read it has run, the warpgroup may write the next P into it
+    B_OFULL = 17,
+    B_OFREE = 18,   // the epilogue has O in registers: the next item's P V may overwrite the accumulator
+    B_QEMPTY = 19,  // every Q K^T of the item has run: the next item's Q may be loaded
+    B_SFREE = 20,   // [S buffer]: its scores are in the softmax warpgroup's registers, Q K^T may overwrite it
+    B_PFREE = 22,   // [P buffer]: the P V that read it has run, the warpgroup may write the next P into it
     // Rings of two slots between the warpgroups, one use per item with two or more tiles:
-    B_MRFULL = 22,  // [slot] the row references of the item's first tile are in shared memory
-    B_MREMPTY = 24, // [slot] ... and have been read by the owner of the item's second tile
-    B_LSFULL = 26,  // [slot] both warpgroups' partial row sums of an item are in shared memory (one use per item)
-    B_LSEMPTY = 28, // [slot] ... and the epilogue warpgroup has read them
-    B_COUNT = 30
+    B_MRFULL = 24,  // [slot] the row references of the item's first tile are in shared memory
+    B_MREMPTY = 26, // [slot] ... and have been read by the owner of the item's second tile
+    B_LSFULL = 28,  // [slot] both warpgroups' partial row sums of an item are in shared memory (one use per item)
+    B_LSEMPTY = 30, // [slot] ... and the epilogue warpgroup has read them
+    B_COUNT = 32
 };
 
 __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
@@ -112,7 +116,8 @@ __device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] 
 // [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
 __device__ unsigned long long g_prof[24];
 __device__ int g_prof_on;
-__device__ unsigned long long g_tl[8 * 24];  // profile build: CTA 0's event times, [round][event]
+__device__ unsigned long long g_tl[8 * 24];
+__device__ unsigned long long g_cta_t[2 * 160];   // profile build: each CTA's entry and exit time (globaltimer, ns)  // profile build: CTA 0's event times, [round][event]
 #ifndef DLX_TC5_PROFILE
 #define DLX_TC5_PROFILE 0   // 1 compiles the cycle accounting in (it perturbs the single MMA-issuing thread)
 #endif
@@ -145,11 +150,35 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
         if (mbar_try(bar, parity)) return true;
         if ((it & 255u) == 255u && *abort_flag) return false;
+#if DLX_WAIT_SLEEP_A
+        // Waiters that are far ahead of (or behind) the critical path poll rarely: a spinning warp takes issue slots
+        // from the softmax warp on its SM sub-partition.
+        if (role == 12 || role == 3 || role == 5 || role == 6) __nanosleep(DLX_WAIT_SLEEP_A);
+#endif
+#if DLX_WAIT_SLEEP_B
+        if (role >= 7 && role <= 11) __nanosleep(DLX_WAIT_SLEEP_B);
+#endif
     }
     *abort_flag = 1 | ((tile & 0xffff) << 8) | (role << 24);
     return false;
 }
 
+// fp32 pair -> bf16x2 on the integer pipe (round half up: add 0x8000, keep the high halves).  The cvt instruction
+// shares the quarter-rate pipe with ex2, which is the pipe that bounds the softmax; P is positive and finite, so
+// half-up differs from round-to-nearest-even only on exact ties.  PACK_ALU_OF4 of every 4 pairs go this way.
+#ifndef DLX_WAIT_SLEEP_A
+#define DLX_WAIT_SLEEP_A 0
+#endif
+#ifndef DLX_WAIT_SLEEP_B
+#define DLX_WAIT_SLEEP_B 0
+#endif
+#ifndef DLX_PACK_ALU_OF4
+#define DLX_PACK_ALU_OF4 0
+#endif
+constexpr int PACK_ALU_OF4 = DLX_PACK_ALU_OF4;
+__device__ __forceinline__ uint32_t pack2_alu(float lo, float hi) {
+    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
 template <int N> __device__ __forceinline__ void reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
 template <int N> __device__ __forceinline__ void reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
@@ -329,9 +358,20 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
 #if DLX_TC5_PROFILE
     const long long t_entry = clock64();
     const bool tl_on = g_prof_on && blockIdx.x == 0;
-#define DLX_STAMP(i) do { if (prof_thread() && g_prof[i] == 0) g_prof[i] = (unsigned long long)(clock64() - t_entry); } while (0)
+    if (g_prof_on && threadIdx.x == 0 && blockIdx.x < 160) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_cta_t[blockIdx.x] = t; }
+#define DLX_TL0(ev) do { if (tl_on) g_tl[(ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
 #else
-#define DLX_STAMP(i) do { } while (0)
+#define DLX_TL0(ev) do { } while (0)
+#endif
+#if DLX_TC5_PROFILE
+#define DLX_TI(base, k) do { if (tl_on && (kq == 40 || kq == 41)) g_tl[6 * 24 + (base) + (kq - 40) * 5 + (k)] = (unsigned long long)(clock64() - t_entry); } while (0)
+#else
+#define DLX_TI(base, k) do { } while (0)
+#endif
+#if DLX_TC5_PROFILE
+#define DLX_TT(k) do { if (tl_on && (jj == 40 || jj == 41) && L == 0) g_tl[7 * 24 + w * 12 + (k)] = (unsigned long long)(clock64() - t_entry); } while (0)
+#else
+#define DLX_TT(k) do { } while (0)
 #endif
 #if DLX_TC5_PROFILE
 #define DLX_TL(ev) do { if (tl_on && round < 8) g_tl[round * 24 + (ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
@@ -354,6 +394,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         uint32_t* dst = reinterpret_cast<uint32_t*>(gbase + OFF_ARGS);
         if (tid < (int)(sizeof(DecodeArgs) / 4)) dst[tid] = src[tid];
         __syncthreads();
+        if (tid == 0) DLX_TL0(21);
     }
     const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);
     const int G = a.group;
@@ -389,6 +430,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // lengths -> offsets, ~2 us) is paid once per CTA instead of once per item and role.
     Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
     if (TABLE && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
+    if (tid == 0) DLX_TL0(22);
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
     int2* rowmap = reinterpret_cast<int2*>(gbase + OFF_ROWMAP);
@@ -420,7 +462,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (tid == 0) DLX_STAMP(16);
+    if (tid == 0) DLX_TL0(23);
     // Running totals over the valid items this CTA has finished (identical in every role):
     //   done = items, ck = key tiles.  Tile k of an item has running index ck + k: S/P buffer (ck + k) & 1, and
     //   (ck + k) >> 1 earlier uses of that buffer.
@@ -474,9 +516,11 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
 #pragma unroll 1
             for (int jj = jj_first; jj < n && alive; jj += 2) {
                 const int u = (ck + jj) >> 1;              // use count of this warpgroup's buffers: phase of their barriers
+                DLX_TT(0);
                 bool ok = mbar_wait(bar(B_SFULL + w), u & 1, abort_flag, 1 + w, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
+                DLX_TT(1);
                 if (jj == jj_first && L == 0) DLX_TL(w ? 6 : 1);
                 // Ring bookkeeping of the row reference (all warps, valid rows or not, keep the barrier counts whole):
                 // the owner of tile 0 fills the slot, the owner of tile 1 drains it.
@@ -509,6 +553,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
+                    DLX_TT(2);
                     float mx4[4];  // four independent chains: the max is latency-, not issue-bound
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -553,6 +598,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     }
                     tc_fence_before();
                     mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
+                    DLX_TT(3);
                     if (u >= 1) {
                         // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
                         // this buffer must have been consumed before the next one goes in (and before this barrier's
@@ -560,6 +606,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
                         if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
                     }
+                    DLX_TT(4);
                     // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
@@ -571,13 +618,15 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            pk[e >> 1] = (((e >> 1) & 3) < PACK_ALU_OF4) ? pack2_alu(p.x, p.y) : pack2<__nv_bfloat16>(p.x, p.y);
                         }
                         tmem_st16(tP + c * 16, pk);
                     }
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     l_run += lacc0.x + lacc0.y;
+                    DLX_TT(5);
                     tmem_st_wait();
+                    DLX_TT(6);
                 } else {
                     // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
                     // arrival for a later tile landing in the phase of this one would complete that phase early.
@@ -814,13 +863,31 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     }
                     __syncwarp();
                 }
-                bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                // Everything a whole-tile copy needs is worked out BEFORE the wait for the ring slot: what follows the wait
+                // is on the critical path of a two- or three-deep ring (slot freed -> copy issued -> data -> MMA).
                 const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
                 const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
-                if (jj == 0 && lane == 0) DLX_TL(14 + which);
                 const CUtensorMap* lvl_maps = which ? maps.v : maps.k;
-                if (by_tma || tma_rows > 0) {
+                const bool one_box = by_tma && a.tma_box_rows == TILE_N;   // the tile is one box (pair) of one page
+                const int pid0 = (one_box && pj < a.max_blocks) ? bt[pj] : -1;   // a bad id is out of bounds: zero fill
+#if DLX_TC5_PROFILE
+                if (tl_on && jj == 40 && lane == 0) g_tl[5 * 24 + which * 6 + 0] = (unsigned long long)(clock64() - t_entry);
+#endif
+                bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
+#if DLX_TC5_PROFILE
+                if (tl_on && jj == 40 && lane == 0) g_tl[5 * 24 + which * 6 + 1] = (unsigned long long)(clock64() - t_entry);
+#endif
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                if (jj == 0 && lane == 0) DLX_TL(14 + which);
+                if (one_box) {
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(full, ITEM_BYTES);
+                        tma_load_4d(d0, &lvl_maps[0], 0, kvh, prow, pid0, full);
+                        tma_load_4d(d0 + REGION, &lvl_maps[0], 64, kvh, prow, pid0, full);
+                    } else {
+                        mbar_arrive(full);
+                    }
+                } else if (by_tma || tma_rows > 0) {
                     if (lane == 0) {
                         const int rows_by_tma = by_tma ? TILE_N : tma_rows;
                         if (by_tma) mbar_arrive_expect_tx(full, ITEM_BYTES);
@@ -841,6 +908,14 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         mbar_arrive(full);
                     }
                 }
+#if DLX_TC5_PROFILE
+                if (tl_on && jj == 40 && lane == 0) {   // when did the copy land?  (polls the full barrier: profile build only)
+                    g_tl[5 * 24 + which * 6 + 2] = (unsigned long long)(clock64() - t_entry);
+                    const uint32_t par_full = (idx / stages) & 1;
+                    for (int spin = 0; spin < 100000 && !mbar_try(full, par_full); ++spin) { }
+                    g_tl[5 * 24 + which * 6 + 3] = (unsigned long long)(clock64() - t_entry);
+                }
+#endif
                 if (!by_tma) {
                     const uint32_t dbase = d0 + half_off;
                     const int pairs = (c_end - tma_rows + 1) >> 1;
@@ -889,12 +964,16 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // S buffer and its use count
+                const int kq = k;
+                DLX_TI(10, 0);
                 if (u >= 1) {
                     ok = mbar_wait(bar(B_SFREE + b), (u - 1) & 1, abort_flag, 11, k);
                     if (!ok) break;
                 }
+                DLX_TI(10, 1);
                 ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
                 if (!ok) break;
+                DLX_TI(10, 2);
                 fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
                 tc_fence_after();
                 const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
@@ -905,6 +984,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
                 }
                 tc_commit(bar(B_SFULL + b));
+                DLX_TI(10, 3);
                 tc_commit(bar(B_KEMPTY + idx % KSTAGES));
             }
             if (ok) tc_commit(bar(B_QEMPTY));   // every Q K^T of this item has read Q
@@ -931,9 +1011,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // P buffer and its use count
-                ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k) &&
-                     mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
+                const int kq = k;
+                DLX_TI(0, 0);
+                ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k);
+                DLX_TI(0, 1);
+                ok = ok && mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                 if (!ok) break;
+                DLX_TI(0, 2);
                 if (k == 0) DLX_TL(12);
                 fence_async_proxy();
                 tc_fence_after();
@@ -943,6 +1027,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(bar(B_PFREE + b));
+                DLX_TI(0, 3);
                 tc_commit(bar(B_VEMPTY + idx % VSTAGES));
             }
             if (ok) tc_commit(bar(B_OFULL));
@@ -955,6 +1040,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
+#if DLX_TC5_PROFILE
+    if (g_prof_on && tid == 0 && blockIdx.x < 160) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_cta_t[160 + blockIdx.x] = t; }
+#endif
     if (tid == 0 && *abort_flag != 0) {   // a wait ran out: record where (the first CTA to report wins)
         const int word = *abort_flag;
         if (atomicCAS(&g_status[0], 0, 1) == 0) {
@@ -1108,6 +1196,7 @@ int read_tc5_status(int out[4]) {
 #if DLX_TC5_PROFILE
 extern "C" int dlx_debug_timeline(unsigned long long* out) {   // profile build only: copies out and clears [8][16] event times
     cudaError_t e = cudaMemcpyFromSymbol(out, tc5::g_tl, sizeof(unsigned long long) * 192);
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(out + 192, tc5::g_cta_t, sizeof(unsigned long long) * 320);
     unsigned long long zero[192] = {};
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_tl, zero, sizeof(zero));
     return e == cudaSuccess ? DLX_OK : DLX_ERR_CUDA;
