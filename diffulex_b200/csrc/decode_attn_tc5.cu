@@ -203,6 +203,11 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
 }
+// The same kind of box, global -> L2 only.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
@@ -392,15 +397,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     {
         const uint32_t* src = reinterpret_cast<const uint32_t*>(&a_param);
         uint32_t* dst = reinterpret_cast<uint32_t*>(gbase + OFF_ARGS);
-        if (tid < (int)(sizeof(DecodeArgs) / 4)) dst[tid] = src[tid];
-        __syncthreads();
-        if (tid == 0) DLX_TL0(21);
+        if (tid < (int)(sizeof(DecodeArgs) / 4)) dst[tid] = src[tid];   // visible after the set-up barrier below
     }
-    const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);
-    const int G = a.group;
+    const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);   // for use AFTER the set-up barrier
+    const int G = a_param.group;
 
     if (tid == 0) {
-        mbar_init(bar(B_QFULL), a.q_by_tma ? 1 : NUM_LOADERS);
+        mbar_init(bar(B_QFULL), a_param.q_by_tma ? 1 : NUM_LOADERS);
         mbar_init(bar(B_QEMPTY), 1);
         for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), NUM_LOADERS); mbar_init(bar(B_KEMPTY + s), 1); }
         for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
@@ -417,19 +420,20 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    const int n_rounds = (a.items_total + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int items_total = a_param.items_total;
+    const int n_rounds = (items_total + (int)gridDim.x - 1) / (int)gridDim.x;
     // Round k of the item list goes to the CTAs in alternating direction (0..G-1, then G-1..0, ...): with the list
     // sorted longest-first this evens out the CTAs' totals, and the two row blocks of one (sequence, KV head),
     // neighbours in the list, still run at the same time on neighbouring CTAs and share their K/V through L2.
     auto item_of_round = [&](int k) {
         const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
         const int item = k * (int)gridDim.x + c;
-        return item < a.items_total ? item : -1;
+        return item < items_total ? item : -1;
     };
     // All rounds are decoded up front, one thread per round: the chain of dependent metadata loads (sequence order ->
     // lengths -> offsets, ~2 us) is paid once per CTA instead of once per item and role.
     Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
-    if (TABLE && tid < n_rounds) items_s[tid] = load_item(a, item_of_round(tid));
+    if (TABLE && tid < n_rounds) items_s[tid] = load_item(a_param, item_of_round(tid));
     if (tid == 0) DLX_TL0(22);
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
@@ -442,17 +446,32 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     {
         // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
         // by a Q box: zero them once, so that the unused TMEM lanes only ever see finite scores.
-        const int rows_used = a.q_tokens * G;
+        const int rows_used = a_param.q_tokens * G;
         for (int i = tid; i < (TILE_M - rows_used) * 16; i += NUM_THREADS) {
             const int row = rows_used + (i >> 4), chunk = i & 15;
             *reinterpret_cast<uint4*>(gbase + (chunk >> 3) * REGION + row * 128 + ((chunk & 7) << 4)) = make_uint4(0, 0, 0, 0);
         }
         // The K and V rings start out as zeros: rows that no copy writes (past the last key of a tail tile) must hold
         // finite values, because 0 x NaN would poison the P V product.
-        if (a.tma_box_rows > 0)
+        if (a_param.tma_box_rows > 0)
             for (int i = tid; i < (KSTAGES + VSTAGES) * ITEM_BYTES / 16; i += NUM_THREADS)
                 *reinterpret_cast<uint4*>(gbase + OFF_K + i * 16) = make_uint4(0, 0, 0, 0);
         fence_async_proxy();
+    }
+    // The loader warps fetch the page ids of the CTA's first item already now, next to the table fill above (their
+    // own decode of the item): otherwise this third dependent load would start only after the set-up barrier.
+    bool bt_preloaded = false;
+    if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
+        const Item f = load_item(a_param, item_of_round(0));
+        if (f.valid) {
+            const int pages = min((f.ctx + a_param.page_size - 1) / a_param.page_size, a_param.max_blocks);
+            if (pages <= BT_SLOTS) {
+                const int32_t* bt_g = a_param.block_tables + (int64_t)f.seq * a_param.bt_stride;
+                int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT) + (warp == VLOAD_WARP ? BT_SLOTS : 0);
+                for (int j = lane; j < pages; j += 32) bt_s[j] = bt_g[j];
+                bt_preloaded = true;
+            }
+        }
     }
     if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
@@ -553,6 +572,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
+                    tc_fence_before();
+                    mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
                     DLX_TT(2);
                     float mx4[4];  // four independent chains: the max is latency-, not issue-bound
 #pragma unroll
@@ -579,25 +600,15 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
                     if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
-                        // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores in TMEM, flag it in
-                        // the device status word, and reload.  Rolled and rare, like the mask pre-pass.
+                        // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores (in registers) and flag
+                        // it in the device status word.  Rare.
                         atomicOr(&g_status[0], 2);
                         const float cap = (m_ref + RAISE_LIMIT) / sl2;
-#pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t wv[32];
-                            tmem_ld32(tS + c * 32, wv);
-                            tmem_ld_wait();
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) wv[e] = __float_as_uint(fminf(__uint_as_float(wv[e]), cap));
-                            tmem_st32(tS + c * 32, wv);
-                        }
-                        tmem_st_wait();
-                        tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
-                        tmem_ld_wait();
+                        for (int c = 0; c < 4; ++c)
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[c][e] = __float_as_uint(fminf(__uint_as_float(v[c][e]), cap));
                     }
-                    tc_fence_before();
-                    mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
                     DLX_TT(3);
                     if (u >= 1) {
                         // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
@@ -791,7 +802,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
             const bool bt_in_smem = pages_needed <= BT_SLOTS;
             __syncwarp();
-            if (bt_in_smem)
+            if (bt_in_smem && !(round == 0 && bt_preloaded))
                 for (int j = lane; j < pages_needed; j += 32) bt_s[j] = bt_g[j];
             const int32_t* bt = bt_in_smem ? bt_s : bt_g;
             __syncwarp();
@@ -957,6 +968,17 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
                 tma_load_3d(sQ, &maps.q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
                 tma_load_3d(sQ + REGION, &maps.q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
+                // The NEXT item's Q goes to L2 now (two prefetch boxes): its copy into the single Q buffer can only
+                // start after this item's last Q K^T, and should then not have to wait for DRAM.
+                if constexpr (TABLE) {
+                    for (int r2 = round + 1; r2 < n_rounds; ++r2) {
+                        const Item nx = items_s[r2];
+                        if (!nx.valid) continue;
+                        tma_prefetch_3d(&maps.q, 0, nx.kvh * G, nx.q0 + nx.tok0);
+                        tma_prefetch_3d(&maps.q, 64, nx.kvh * G, nx.q0 + nx.tok0);
+                        break;
+                    }
+                }
             }
             ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
             DLX_TL(9);
