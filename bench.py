@@ -46,7 +46,7 @@ import torch
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch from the committed ncu captures
 # (profiles/), keyed by workload; None until a capture exists for that workload.
-NCU_TRAFFIC_BYTES = {"cfg2": 178001152 + 10541824}  # profiles/decode_attn_tc5_cfg2.md
+NCU_TRAFFIC_BYTES = {"cfg2": 178767616 + 7958784}  # profiles/decode_attn_tc5_cfg2.md
 
 
 def parse():
@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--num-splits", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-store-load", action="store_true", help="skip the store / load bandwidth side measurement")
     return ap.parse_args()
 
 
@@ -134,6 +135,67 @@ def cpu_attention_baseline(w, budget_s=12.0):
     dt = statistics.median(times)
     return (p.kv_bytes() / dt / 1e9, int(p.host_new_lens.sum()) / dt, cores,
             f"1 of {w.geometry.layers} layers, all {p.num_seqs} sequences, fp32, {len(times)} runs, median")
+
+
+def store_load_bandwidth(dlx, dev, peak):
+    """Store and load kernels on one cfg5-shaped layer (256 sequences, ctx U[4096, 32768]: 9.7 GB of KV, far
+    larger than L2).  Algorithmic bytes: store N_valid * row * 2 (K and V) * 2 (read + write) + N * sizeof(slot);
+    load rows * row * 2 * 2.  Three cases: the per-step store of the in-flight blocks (N = 8192), a prefill-sized
+    store (every cached token of the layer) and the load of every sequence's [prefix ; in-flight] rows."""
+    from diffulex_b200.workload import make_problem, named_workload
+    p = make_problem(named_workload("cfg5"), device=dev, values="torch")
+    geo = p.geometry
+    row = geo.num_kv_heads * geo.head_dim * 2
+    md = p.metadata("varlen")
+
+    def timed(fn, iters):
+        fn(); torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record(); torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1e-3
+
+    n_step = p.k.shape[0]
+    # the per-step store is a 35 MB copy: replayed from a CUDA graph (20 launches) so that host launch time is out
+    store_step = lambda: dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        store_step()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(20):
+            store_step()
+    t_step = timed(g.replay, 5) / 20
+    # prefill-sized: one row per cached token, written to the slot it already occupies
+    slots = []
+    bt, ctx = p.block_tables.cpu(), p.host_context_lens
+    for s in range(p.num_seqs):
+        pos = torch.arange(int(ctx[s]))
+        slots.append(bt[s][pos // geo.page_size].long() * geo.page_size + pos % geo.page_size)
+    slots = torch.cat(slots).to(torch.int32).to(dev)
+    n_big = slots.numel()
+    kb = torch.empty(n_big, geo.num_kv_heads, geo.head_dim, dtype=p.k.dtype, device=dev).normal_()
+    vb = torch.empty_like(kb).normal_()
+    t_big = timed(lambda: dlx.store_kvcache_unified_layout(kb, vb, p.k_cache, p.v_cache, slots, md), 3)
+    del kb, vb
+    rows = int(p.host_context_lens.sum() + p.host_new_lens.sum())
+    md.total_kv_rows = rows
+    t_load = timed(lambda: dlx.load_kvcache(p.k_cache, p.v_cache, md, p.k, p.v), 3)
+    gb = lambda b, t: b / t / 1e9
+    out = {
+        "workload": "cfg5-shaped layer: 256 seqs, ctx U[4096,32768], 28q/4kv x 128, page 256",
+        "store_step": {"tokens": n_step, "us": t_step * 1e6, "gbps": gb(n_step * (row * 4 + 4), t_step)},
+        "store_prefill_sized": {"tokens": n_big, "ms": t_big * 1e3, "gbps": gb(n_big * (row * 4 + 4), t_big)},
+        "load": {"rows": rows, "ms": t_load * 1e3, "gbps": gb(rows * row * 4, t_load)},
+        "peak_gbps": peak,
+    }
+    for k in ("store_step", "store_prefill_sized", "load"):
+        out[k]["frac_of_peak"] = out[k]["gbps"] / peak
+    return out
 
 
 def run_reference(args, w, rank, world):
@@ -337,6 +399,13 @@ def main():
         e2e = {"value": tot / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e, "ms_per_step": ms_e2e / n_e2e}
 
+    # ---- side measurement (rank 0, one GPU): store and load bandwidth on a cfg5-shaped layer ----
+    store_load = None
+    if rank == 0 and world == 1 and not args.no_store_load:
+        del layers, graph, g_dec
+        torch.cuda.empty_cache()
+        store_load = store_load_bandwidth(dlx, dev, peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, toks, cores, sample = cpu_attention_baseline(w_global)
@@ -360,7 +429,7 @@ def main():
                        "l2": f"inputs larger than L2: {L} distinct layer caches, "
                              f"{kv_bytes_layer * L / 1e9:.2f} GB of KV per step",
                        "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.scaling})")},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "store_load": store_load,
             "gpu_launches": args.steps * L * launches_per_layer, "clocks": clocks, "per_rank_ms": per_rank_ms,
         }
         print(json.dumps(line))

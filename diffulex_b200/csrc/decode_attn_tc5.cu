@@ -1,31 +1,28 @@
-// Paged block-diffusion decode attention on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Paged block-diffusion decode attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// Shape served: head_dim 128, bf16, 128 < G * q_len <= 256 packed query rows per KV head (e.g.
-// 28 query heads over 4 KV heads with a 32-token diffusion block: 224 rows).  One CTA owns
-// (sequence, KV head, key-range split) and keeps TWO 128-row Q tiles resident, so every K/V tile
-// is fetched from HBM once and used by both: at ~224 flop per KV byte the legacy mma.sync pipe is
-// the limiter, the tcgen05 pipe is not.
+// Shape served: head_dim 128, bf16, any number G <= 128 of query heads per KV head.  All G heads of a KV head are
+// packed into the M dimension, so every K/V byte is read once per GROUP of heads.
 //
-// Warp roles (352 threads, up to 184 registers each so a softmax thread holds its whole S row):
-//   warps 0-3   softmax warpgroup of Q tile 0: thread <-> TMEM lane <-> query row
-//   warps 4-7   softmax warpgroup of Q tile 1
-//   warps 8-9   loaders.  K/V tiles (128 keys) that lie wholly inside the cached prefix are fetched by
-//               TMA (cp.async.bulk.tensor, 4-D map {hd, Hkv, page row, page} with 128-byte swizzle, plain
-//               per-CTA loads): one thread issues two boxes per tile and the copy engine keeps far more
-//               bytes in flight than LDGSTS can (16-byte cp.async tops out near 14 B/clk/SM here).
-//               The tile that holds the end of the prefix and the in-flight rows, and every tile when
-//               the page size does not fit a box, go through 16-byte cp.async with the same swizzle:
-//               any page size, prefix and in-flight rows as ONE key axis, rows past the end zero-filled
-//   warp 10     one elected thread issues tcgen05.mma: S_t = Q_t K^T (SS form) into TMEM, and
-//               O_t += P_t V (TS form: P is read from TMEM, V^T from shared memory), and
-//               tcgen05.commit to the mbarriers that hand tiles back and forth
-// TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 fp32 columns each; P_t (bf16) overwrites the first
-// 64 columns of S_t in place.  The two Q tiles ping-pong: while a softmax warpgroup works on S_t
-// the tensor pipe runs the other tile's MMAs.  The running maximum is only raised when it grows by
-// more than 2^8 (the accumulator then is rescaled in TMEM), so most tiles skip the rescale.
+// Work item = (sequence, KV head, block of 128 / G whole query tokens, key-range split).  The kernel is
+// persistent: one CTA per SM walks its share of the (longest-first) item list and keeps every ring and barrier
+// phase running across items, so the next item's Q/K/V land while the current one is finished.
 //
-// Every mbarrier wait is bounded; on expiry the CTA raises an abort flag, records where it gave up
-// in a device status word, drains, frees TMEM and returns (no trap, the context stays usable).
+// Warp roles (512 threads; after the split the warpgroups resize their register files with setmaxnreg):
+//   warps 0-7    two softmax warpgroups over the SAME 128 rows (thread <-> TMEM lane <-> query row), taking
+//                alternate key tiles: S -> registers, row max, P = exp2(s * scale - m_ref) as bf16 -> TMEM.
+//                m_ref is fixed by the item's first tile: no accumulator rescale ever runs
+//   warp 8, 9    K loader, V loader.  Tiles (128 keys) inside the cached prefix come by TMA
+//                (cp.async.bulk.tensor, 4-D map {hd, Hkv, page row, page}, 128-byte swizzle, plain per-CTA
+//                loads).  The tile with the end of the prefix: boxes of 64/32/16/8 rows for its cached rows, 16-byte
+//                cp.async for the < 8 left over and for the in-flight rows.  Page sizes that fit no box: cp.async
+//   warp 10      one thread issues S = Q K^T (tcgen05.mma, SS form) and fetches Q (TMA, one box per head_dim half);
+//                the warp also allocates and frees TMEM
+//   warp 11      one thread issues O += P V (TS form: P from TMEM, V as MN-major B operand from the [key][hd] tile)
+//   warps 12-15  epilogue warpgroup: O / l -> global through a swizzled staging buffer (coalesced rows)
+// TMEM (512 columns): S[2] (128 fp32 columns each) | P[2] (64 columns = 128 bf16 each) | O (128).
+//
+// Every mbarrier wait is bounded; on expiry the CTA raises an abort word, everyone drains, the place is copied to a
+// device status word, TMEM is freed and the CTA returns (no trap, the context stays usable).
 //
 // Reference semantics: diffulex_kernel/python/dllm_flash_attn.py:163-347 and :632-637.
 #include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (resolved at run time, no libcuda link)
@@ -58,7 +55,7 @@ constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
 constexpr int OFF_TAB = OFF_BAR + 512;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
-constexpr int BT_SLOTS = 512;                      // 2 KiB each: 131 k tokens at 256-token pages
+constexpr int BT_SLOTS = 512;                      // 2 KiB per loader warp: 131 k tokens at 256-token pages
 constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 8 x 128 floats: two slots of row references; two slots of (row sums x 2, reference)
 constexpr int OFF_STAGE = OFF_XCH + 8 * 128 * 4;   // output staging: 32 rows x 128 bytes per epilogue warp
 constexpr int STAGE_WARP_BYTES = 32 * 128;
@@ -150,35 +147,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
         if (mbar_try(bar, parity)) return true;
         if ((it & 255u) == 255u && *abort_flag) return false;
-#if DLX_WAIT_SLEEP_A
-        // Waiters that are far ahead of (or behind) the critical path poll rarely: a spinning warp takes issue slots
-        // from the softmax warp on its SM sub-partition.
-        if (role == 12 || role == 3 || role == 5 || role == 6) __nanosleep(DLX_WAIT_SLEEP_A);
-#endif
-#if DLX_WAIT_SLEEP_B
-        if (role >= 7 && role <= 11) __nanosleep(DLX_WAIT_SLEEP_B);
-#endif
     }
     *abort_flag = 1 | ((tile & 0xffff) << 8) | (role << 24);
     return false;
 }
 
-// fp32 pair -> bf16x2 on the integer pipe (round half up: add 0x8000, keep the high halves).  The cvt instruction
-// shares the quarter-rate pipe with ex2, which is the pipe that bounds the softmax; P is positive and finite, so
-// half-up differs from round-to-nearest-even only on exact ties.  PACK_ALU_OF4 of every 4 pairs go this way.
-#ifndef DLX_WAIT_SLEEP_A
-#define DLX_WAIT_SLEEP_A 0
-#endif
-#ifndef DLX_WAIT_SLEEP_B
-#define DLX_WAIT_SLEEP_B 0
-#endif
-#ifndef DLX_PACK_ALU_OF4
-#define DLX_PACK_ALU_OF4 0
-#endif
-constexpr int PACK_ALU_OF4 = DLX_PACK_ALU_OF4;
-__device__ __forceinline__ uint32_t pack2_alu(float lo, float hi) {
-    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
-}
 template <int N> __device__ __forceinline__ void reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
 template <int N> __device__ __forceinline__ void reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
@@ -202,11 +175,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
-}
-// The same kind of box, global -> L2 only.
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n"
-                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2) : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
     asm volatile(
@@ -629,7 +597,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[e >> 1] = (((e >> 1) & 3) < PACK_ALU_OF4) ? pack2_alu(p.x, p.y) : pack2<__nv_bfloat16>(p.x, p.y);
+                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                         }
                         tmem_st16(tP + c * 16, pk);
                     }
@@ -785,7 +753,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         const char* cache = static_cast<const char*>(which ? a.v_cache : a.k_cache);
         const char* fresh = static_cast<const char*>(which ? a.v : a.k);
         const int64_t fresh_rs = which ? a.v_rs : a.k_rs;
-        int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
+        int32_t* bt_base = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
         // Row-source table for tiles that go through cp.async: where each key row's bytes start (nullptr = row past
         // the end, zero-filled).  Four rows per lane; one table per loader warp, rebuilt per tile.
         const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
@@ -799,12 +767,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             const int32_t* bt_g = a.block_tables + (int64_t)it.seq * a.bt_stride;
             // This sequence's page ids go to shared memory once per item (a per-tile global lookup would put an L2 round
             // trip in front of every tile's copies); each loader warp keeps its own copy.  Longer tables stay global.
+            // (Fetching the NEXT item's ids ahead of time, by cp.async or through registers, cost more than it saved.)
             const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
             const bool bt_in_smem = pages_needed <= BT_SLOTS;
             __syncwarp();
             if (bt_in_smem && !(round == 0 && bt_preloaded))
-                for (int j = lane; j < pages_needed; j += 32) bt_s[j] = bt_g[j];
-            const int32_t* bt = bt_in_smem ? bt_s : bt_g;
+                for (int j = lane; j < pages_needed; j += 32) bt_base[j] = bt_g[j];
+            const int32_t* bt = bt_in_smem ? bt_base : bt_g;
             __syncwarp();
             if (which == 1 && !a.q_by_tma) {
                 // Q without TMA (the Q K^T issuer fetches it otherwise): 16-byte cp.async as soon as the last Q K^T of
@@ -968,17 +937,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
                 tma_load_3d(sQ, &maps.q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
                 tma_load_3d(sQ + REGION, &maps.q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
-                // The NEXT item's Q goes to L2 now (two prefetch boxes): its copy into the single Q buffer can only
-                // start after this item's last Q K^T, and should then not have to wait for DRAM.
-                if constexpr (TABLE) {
-                    for (int r2 = round + 1; r2 < n_rounds; ++r2) {
-                        const Item nx = items_s[r2];
-                        if (!nx.valid) continue;
-                        tma_prefetch_3d(&maps.q, 0, nx.kvh * G, nx.q0 + nx.tok0);
-                        tma_prefetch_3d(&maps.q, 64, nx.kvh * G, nx.q0 + nx.tok0);
-                        break;
-                    }
-                }
             }
             ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
             DLX_TL(9);

@@ -113,7 +113,7 @@ def test_load_bit_exact(name, dlx, golden_dir):
 @pytest.mark.parametrize("num_splits", [0, 1, 3])
 @pytest.mark.parametrize("kernel", ["auto", "mma"])
 def test_attention_matches_golden_and_oracle(name, mode, num_splits, kernel, dlx, golden_dir, monkeypatch):
-    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128, up to 256 packed rows)
+    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128)
     # and the mma.sync kernel elsewhere; "mma" forces the mma.sync kernel everywhere
     monkeypatch.setenv("DLX_DECODE_KERNEL", {"auto": "0", "mma": "1"}[kernel])
     meta = json.loads((golden_dir / "attn_golden.json").read_text())[name]
@@ -283,8 +283,8 @@ def test_cfg5_attention_properties(dlx, cfg5_problem):
 
 
 def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
-    """Forcing the tcgen05 kernel works on eligible shapes (head_dim 128, up to 256 packed rows: 224 and
-    16 here), is refused on an ineligible one (head_dim 64), and the kernel's bounded waits never ran
+    """Forcing the tcgen05 kernel works on eligible shapes (head_dim 128: 7 and 4 query heads per KV head
+    here), is refused on an ineligible one (head_dim 64), and the kernel's bounded waits never ran
     out during this test session."""
     import ctypes
     from diffulex_b200 import _lib
@@ -300,6 +300,32 @@ def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
     st = (ctypes.c_int32 * 4)()
     assert _lib.lib().dlx_debug_device_status(st) == 0
     assert list(st) == [0, 0, 0, 0], f"a bounded wait expired: {list(st)}"
+
+
+def test_out_of_range_scores_are_clamped_flagged_and_finite(dlx, monkeypatch):
+    """A key whose score lies more than 100 log2-units above the softmax reference of its row (here ~130 nats
+    above everything else) uses up the exponent headroom of the fixed-reference softmax: the kernel clamps
+    it, sets bit 1 of the device status word, and the output stays finite; with ONE such key the clamped
+    result still equals the exact one (that key's V row)."""
+    import ctypes
+    from diffulex_b200 import _lib
+    from diffulex_b200.workload import MASK_BD_FULL, make_problem, small_workload
+    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
+    w = small_workload("clamp", 28, 4, 128, 64, 32, [300, 520], [32, 32], MASK_BD_FULL, 77)
+    p = make_problem(w, device="cpu", values="numpy")
+    u = p.q[0, 0].clone()
+    p.q[:] = u                                         # every row asks the same question ...
+    for s in range(2):                                 # ... and key 5 of every sequence answers it 12 times over
+        page = int(p.block_tables[s, 0])
+        p.k_cache[page, 5] = (12.0 * u).to(p.k_cache.dtype)
+    st = (ctypes.c_int32 * 4)()
+    assert _lib.lib().dlx_debug_device_status(st) == 0   # clear
+    want = oracle_out(p)
+    o = run_decode(dlx, to_dev(p), "static", 1)
+    assert torch.isfinite(o).all()
+    torch.testing.assert_close(o.float().cpu(), want, atol=ATOL, rtol=RTOL)
+    assert _lib.lib().dlx_debug_device_status(st) == 0   # reads and clears
+    assert st[0] == 2 and list(st)[1:] == [0, 0, 0], f"expected only the clamp flag: {list(st)}"
 
 
 # ---- error behaviour ---------------------------------------------------------------------------
