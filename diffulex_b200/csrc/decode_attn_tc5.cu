@@ -24,6 +24,11 @@
 // Every mbarrier wait is bounded; on expiry the CTA raises an abort word, everyone drains, the place is copied to a
 // device status word, TMEM is freed and the CTA returns (no trap, the context stays usable).
 //
+// Measured on B200 and rejected (each was slower than what is here): L2 prefetch of K/V tiles ahead of the rings,
+// by cp.async.bulk.prefetch.tensor or by prefetch.global.L2; fetching the next item's page ids or Q ahead of time;
+// handing P to the tensor pipe in two halves of 64 keys; packing P to bf16 on the integer pipe; tracking the row
+// maximum inside the exponential loop; a second Q buffer at the price of a K stage; polling waits with nanosleep.
+//
 // Reference semantics: diffulex_kernel/python/dllm_flash_attn.py:163-347 and :632-637.
 #include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (resolved at run time, no libcuda link)
 
@@ -767,7 +772,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             const int32_t* bt_g = a.block_tables + (int64_t)it.seq * a.bt_stride;
             // This sequence's page ids go to shared memory once per item (a per-tile global lookup would put an L2 round
             // trip in front of every tile's copies); each loader warp keeps its own copy.  Longer tables stay global.
-            // (Fetching the NEXT item's ids ahead of time, by cp.async or through registers, cost more than it saved.)
             const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
             const bool bt_in_smem = pages_needed <= BT_SLOTS;
             __syncwarp();

@@ -72,7 +72,9 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
         int64_t want = 1;
         if (units > 0 && units < slots) want = (slots + units - 1) / units;
         const int64_t chunk = 40 * (int64_t)d.mma.block_m > 512 ? 40 * (int64_t)d.mma.block_m : 512;
-        const int64_t by_len = (max_len + chunk - 1) / chunk;
+        // The tcgen05 kernel is persistent (one CTA per SM walks a longest-first item list): with two or more
+        // items per SM the list balances by itself and a split would only add partial writes and the combine.
+        const int64_t by_len = (d.use_tc5 && units >= 2 * slots) ? 1 : (max_len + chunk - 1) / chunk;
         int64_t s = want > by_len ? want : by_len;
         const int64_t cap = max_tiles / 2 > 1 ? max_tiles / 2 : 1;  // at least two key tiles per split
         if (s > cap) s = cap;

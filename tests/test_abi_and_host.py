@@ -96,8 +96,14 @@ def test_split_planning_is_host_only_and_sized_right(lib):
     # few sequences: split to fill 148 SMs
     p = good_params(num_seqs=2, total_q=64)
     assert n(p) > 1
-    # very long contexts are cut even when CTAs abound
+    # long contexts: the persistent tcgen05 kernel balances a long item list by itself (no split) ...
     p = good_params(num_seqs=256, total_q=8192, max_blocks=129)
+    assert n(p) == 1
+    # ... but cuts long contexts while there are fewer than two items per SM
+    p = good_params(num_seqs=24, total_q=768, max_blocks=129)
+    assert n(p) >= 3
+    # the mma.sync kernel launches one CTA per item and keeps cutting long contexts
+    p = good_params(num_seqs=256, total_q=8192, max_blocks=129, kernel=1)
     assert n(p) >= 3
 
 
