@@ -45,7 +45,7 @@ namespace dlx {
 namespace tc5 {
 
 constexpr int HD = 128;
-constexpr int TILE_M = 128;               // packed query rows per CTA (TMEM lanes)
+constexpr int TILE_M = 128;               // packed query rows per work item (TMEM lanes)
 constexpr int TILE_N = 128;               // keys per K/V tile
 constexpr int REGION = 128 * 128;         // [128 rows][64 bf16] 128B-swizzled block: 16 KiB
 constexpr int Q_BYTES = 2 * REGION;       // one Q tile, 2 head_dim halves
@@ -54,7 +54,9 @@ constexpr int ITEM_BYTES = 2 * REGION;    // one K tile or one V tile
 #define DLX_KSTAGES 2
 #define DLX_VSTAGES 3
 #endif
-constexpr int KSTAGES = DLX_KSTAGES, VSTAGES = DLX_VSTAGES;   // Q K^T runs two tiles ahead of P V, so K needs one stage more
+// A ring slot is refilled when its tile has been consumed.  V is consumed late (P V follows the softmax), so it gets
+// the third stage; K is consumed by a Q K^T that already runs two tiles ahead of the softmax (two S buffers).
+constexpr int KSTAGES = DLX_KSTAGES, VSTAGES = DLX_VSTAGES;
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
@@ -113,19 +115,18 @@ enum {
     B_COUNT = 32
 };
 
-__device__ int g_status[4];  // [0] first failure code, [1] role, [2] tile, [3] CTA linear id
-// Optional cycle accounting of CTA (0,0,0): [0] CTA lifetime, [role] cycles spent in that wait site,
-// [12..14] softmax pass 1 / rescale / pass 2 of Q tile 0.  Off unless g_prof_on is set by the host.
-__device__ unsigned long long g_prof[24];
+__device__ int g_status[4];  // [0] bit 0: a bounded wait expired, bit 1: scores were clamped; [1] wait site, [2] tile, [3] CTA
+// Profile build (-DDLX_TC5_PROFILE=1) only: event times of CTA 0, in cycles since its start.  g_tl[round * 24 + event]
+// for rounds 0..4 (item-level events), rows 5..7 hold loader / issuer / softmax stamps of one mid-item tile;
+// g_cta_t holds every CTA's entry and exit time (globaltimer, ns).  Recording is switched on by the host
+// (dlx_debug_profile(1, ...)); the regular build compiles none of it.
+__device__ unsigned long long g_prof[24];   // legacy counters behind dlx_debug_profile's output argument (unused, zero)
 __device__ int g_prof_on;
 __device__ unsigned long long g_tl[8 * 24];
-__device__ unsigned long long g_cta_t[2 * 160];   // profile build: each CTA's entry and exit time (globaltimer, ns)  // profile build: CTA 0's event times, [round][event]
+__device__ unsigned long long g_cta_t[2 * 160];
 #ifndef DLX_TC5_PROFILE
-#define DLX_TC5_PROFILE 0   // 1 compiles the cycle accounting in (it perturbs the single MMA-issuing thread)
+#define DLX_TC5_PROFILE 0
 #endif
-__device__ __forceinline__ bool prof_thread() {
-    return false;   // the per-wait cycle accounting is retired; the profile build records event times instead
-}
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
@@ -317,44 +318,37 @@ __device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
 // warpgroup waits for: a full tile delivers them sooner, while the other warpgroup masks the last tile.
 __device__ __forceinline__ int tile_of(int jj, int n) { return n - 1 - ((jj < 2 && n >= 2) ? (jj ^ 1) : jj); }
 
-// Persistent kernel: one CTA per SM walks work items c, c + gridDim.x, ... of the (longest-first) item list.
-// Every role keeps running counters for the rings and buffers, so the pipeline never drains between items:
-// while the softmax warpgroups finish item i the loaders already fetch Q / K / V of item i + 1 and the Q K^T
-// issuer fills its first two S buffers.
 // Tensor maps of one launch: the K and V caches as {head_dim, Hkv, page row, page} with boxes of 128 >> level rows
 // (level 0..4: 128, 64, 32, 16, 8 rows; levels whose box would exceed a page are unused), and Q.
 struct TmaMaps {
     CUtensorMap k[5], v[5], q;
 };
 
+// Persistent kernel: one CTA per SM walks its rounds of the (longest-first) item list.  Every role keeps running
+// counters for the rings and buffers, so the pipeline never drains between items: while the softmax warpgroups
+// finish item i the loaders already fetch K / V of item i + 1 and the Q K^T issuer fills its first two S buffers.
 // TABLE: the CTA's rounds fit the shared-memory item table (the usual case); otherwise every role decodes its items
 // itself, at the price of five inlined copies of the decoder, which is why that is a separate instantiation.
 template <bool TABLE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps maps) {
     extern __shared__ unsigned char smem_raw[];
+    // Event stamps of the profile build (cycles since CTA 0 started): DLX_TL0 set-up events, DLX_TL item-level events
+    // of round `round`, DLX_TT / DLX_TI softmax / issuer events of tiles 40 and 41 of an item.  Empty otherwise.
 #if DLX_TC5_PROFILE
     const long long t_entry = clock64();
     const bool tl_on = g_prof_on && blockIdx.x == 0;
     if (g_prof_on && threadIdx.x == 0 && blockIdx.x < 160) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_cta_t[blockIdx.x] = t; }
-#define DLX_TL0(ev) do { if (tl_on) g_tl[(ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
+#define DLX_STAMP_AT(idx) g_tl[(idx)] = (unsigned long long)(clock64() - t_entry)
+#define DLX_TL0(ev) do { if (tl_on) DLX_STAMP_AT(ev); } while (0)
+#define DLX_TL(ev) do { if (tl_on && round < 5) DLX_STAMP_AT(round * 24 + (ev)); } while (0)
+#define DLX_TI(base, k) do { if (tl_on && (kq == 40 || kq == 41)) DLX_STAMP_AT(6 * 24 + (base) + (kq - 40) * 5 + (k)); } while (0)
+#define DLX_TT(k) do { if (tl_on && (jj == 40 || jj == 41) && L == 0) DLX_STAMP_AT(7 * 24 + w * 12 + (k)); } while (0)
 #else
 #define DLX_TL0(ev) do { } while (0)
-#endif
-#if DLX_TC5_PROFILE
-#define DLX_TI(base, k) do { if (tl_on && (kq == 40 || kq == 41)) g_tl[6 * 24 + (base) + (kq - 40) * 5 + (k)] = (unsigned long long)(clock64() - t_entry); } while (0)
-#else
-#define DLX_TI(base, k) do { } while (0)
-#endif
-#if DLX_TC5_PROFILE
-#define DLX_TT(k) do { if (tl_on && (jj == 40 || jj == 41) && L == 0) g_tl[7 * 24 + w * 12 + (k)] = (unsigned long long)(clock64() - t_entry); } while (0)
-#else
-#define DLX_TT(k) do { } while (0)
-#endif
-#if DLX_TC5_PROFILE
-#define DLX_TL(ev) do { if (tl_on && round < 8) g_tl[round * 24 + (ev)] = (unsigned long long)(clock64() - t_entry); } while (0)
-#else
 #define DLX_TL(ev) do { } while (0)
+#define DLX_TI(base, k) do { } while (0)
+#define DLX_TT(k) do { } while (0)
 #endif
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -395,7 +389,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     }
     const int items_total = a_param.items_total;
     const int n_rounds = (items_total + (int)gridDim.x - 1) / (int)gridDim.x;
-    // Round k of the item list goes to the CTAs in alternating direction (0..G-1, then G-1..0, ...): with the list
+    // Round k of the item list goes to the CTAs in alternating direction (CTA 0..C-1, then C-1..0, ...): with the list
     // sorted longest-first this evens out the CTAs' totals, and the two row blocks of one (sequence, KV head),
     // neighbours in the list, still run at the same time on neighbouring CTAs and share their K/V through L2.
     auto item_of_round = [&](int k) {
@@ -477,7 +471,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         float* xm = reinterpret_cast<float*>(gbase + OFF_XCH);    // [2][128] row references, ring of two items
         float* xs = xm + 256;                                     // [2][3][128] per item: row sums of each warpgroup, reference
         const float sl2 = a.scale_log2;
-        int mr = 0;                                    // items with two or more tiles so far: position in both rings
+        int mr = 0;                                    // items with two or more tiles so far: position in the m_ref ring
         bool alive = true;
 #pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
