@@ -83,9 +83,9 @@ constexpr int NUM_THREADS = 512;
 // Registers per thread after the roles split (the kernel starts with 65536 / 512 = 128 each): the four helper warps
 // and the epilogue warpgroup give registers back, the two softmax warpgroups (a row of 128 scores each) take them.
 #ifndef DLX_SOFTMAX_REGS
-#define DLX_SOFTMAX_REGS 176
-#define DLX_HELPER_REGS 64
-#define DLX_EPI_REGS 96
+#define DLX_SOFTMAX_REGS 184
+#define DLX_HELPER_REGS 56
+#define DLX_EPI_REGS 88
 #endif
 constexpr int SOFTMAX_REGS = DLX_SOFTMAX_REGS, HELPER_REGS = DLX_HELPER_REGS, EPI_REGS = DLX_EPI_REGS;
 static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget");
