@@ -75,6 +75,15 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak_tflops():
+    """Measured dense bf16 peak (burst figure: the decode kernel is timed launch by launch), if the file gives one."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["bf16_tflops"])
+    except Exception:
+        return None
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons, sampled while the timed region runs."""
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -339,6 +348,10 @@ def main():
                 "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "decode attention (+ combine if split)",
                 "algorithmic_bytes_per_launch": kv_bytes_layer, "avg_launch_us": avg_launch_ms * 1e3,
                 "min_launch_us": min(launch_ms) * 1e3, "tflops": flops_layer / (avg_launch_ms * 1e-3) / 1e12}
+    tensor_peak = tensor_peak_tflops()   # the second fraction asked for on cfg2 / cfg5: tensor-pipe use of the kernel
+    if tensor_peak:
+        roofline["tensor_frac"] = roofline["tflops"] / tensor_peak
+        roofline["tensor_peak_tflops"] = tensor_peak
 
     # ---- e2e: host buffers in, host buffers out, every step ----
     e2e = None
