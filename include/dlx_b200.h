@@ -171,19 +171,21 @@ int64_t dlx_static_scratch_bytes(void);
 int dlx_decode_attn_static_scratch(const dlx_decode_attn_params* p, void* stream);
 
 /*
- * Debug aid with no counterpart in the reference.  Every wait inside the tcgen05 kernel is bounded;
- * a wait that runs out makes its CTA stop early and records {1, role, tile, cta} in a device status
- * word instead of trapping.  This call synchronises the device, copies the word to the HOST array
- * `out` and clears it.  out[0] == 0 means no wait ever expired.
+ * Debug aid with no counterpart in the reference.  out[0] is a bit set: bit 0 = a bounded wait inside the
+ * tcgen05 kernel expired (every wait there is bounded; the CTA then stops early instead of trapping, and
+ * out[1..3] hold the wait site, the tile and the CTA that gave up first); bit 1 = scores more than 100
+ * log2-units above the softmax reference of their row (the row maximum of the first key tile) were
+ * clamped there: the kernel never rescales its accumulator, so that is its exponent headroom.  This call
+ * synchronises the device, copies the word to the HOST array `out` and clears it.  out[0] == 0: neither
+ * happened since the last call.
  */
 int dlx_debug_device_status(int32_t out[4]);
 
 /*
- * Debug aid with no counterpart in the reference: cycle accounting inside the tcgen05 kernel.  While
- * enabled, CTA (0,0,0) of every launch adds clock64() deltas to a device array: [0] CTA lifetime,
- * [1..11] cycles spent at each mbarrier wait site, [12..14] softmax pass 1 / accumulator rescale /
- * pass 2 of Q tile 0.  The call synchronises, copies the array to the HOST array `out` (may be
- * NULL), clears it, and sets the switch to `enable`.
+ * Debug aid with no counterpart in the reference: the switch of the kernel's event recording.  Only a
+ * library built with -DDLX_TC5_PROFILE=1 records anything (CTA 0's event times, every CTA's entry and exit
+ * time); in the regular build the switch is inert.  The call synchronises, copies 24 legacy counters
+ * (all zero) to the HOST array `out` (may be NULL), clears them, and sets the switch to `enable`.
  */
 int dlx_debug_profile(int enable, uint64_t out[24]);
 
