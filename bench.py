@@ -62,6 +62,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-store-load", action="store_true", help="skip the store / load bandwidth side measurement")
+    ap.add_argument("--only-store-load", action="store_true",
+                    help="run only the store / load side measurement and print its object (for profiler captures)")
+    ap.add_argument("--store-load-seqs", type=int, default=256,
+                    help="sequences of the cfg5-shaped layer used by the store / load measurement (256 = all)")
     return ap.parse_args()
 
 
@@ -146,13 +150,19 @@ def cpu_attention_baseline(w, budget_s=12.0):
             f"1 of {w.geometry.layers} layers, all {p.num_seqs} sequences, fp32, {len(times)} runs, median")
 
 
-def store_load_bandwidth(dlx, dev, peak):
+def store_load_bandwidth(dlx, dev, peak, num_seqs=256):
     """Store and load kernels on one cfg5-shaped layer (256 sequences, ctx U[4096, 32768]: 9.7 GB of KV, far
     larger than L2).  Algorithmic bytes: store N_valid * row * 2 (K and V) * 2 (read + write) + N * sizeof(slot);
     load rows * row * 2 * 2.  Three cases: the per-step store of the in-flight blocks (N = 8192), a prefill-sized
     store (every cached token of the layer) and the load of every sequence's [prefix ; in-flight] rows."""
-    from diffulex_b200.workload import make_problem, named_workload
-    p = make_problem(named_workload("cfg5"), device=dev, values="torch")
+    from diffulex_b200.workload import make_problem, named_workload, small_workload
+    w5 = named_workload("cfg5")
+    if num_seqs < len(w5.context_lens):   # a prefix of the same sequences: smaller footprint for profiler captures
+        g5 = w5.geometry
+        w5 = small_workload("cfg5_prefix", g5.num_q_heads, g5.num_kv_heads, g5.head_dim, g5.page_size,
+                            g5.diffusion_block_size, list(w5.context_lens[:num_seqs]), list(w5.new_lens[:num_seqs]),
+                            w5.mask_mode, w5.seed)
+    p = make_problem(w5, device=dev, values="torch")
     geo = p.geometry
     row = geo.num_kv_heads * geo.head_dim * 2
     md = p.metadata("varlen")
@@ -196,7 +206,7 @@ def store_load_bandwidth(dlx, dev, peak):
     t_load = timed(lambda: dlx.load_kvcache(p.k_cache, p.v_cache, md, p.k, p.v), 3)
     gb = lambda b, t: b / t / 1e9
     out = {
-        "workload": "cfg5-shaped layer: 256 seqs, ctx U[4096,32768], 28q/4kv x 128, page 256",
+        "workload": f"cfg5-shaped layer: {p.num_seqs} seqs, ctx U[4096,32768], 28q/4kv x 128, page 256",
         "store_step": {"tokens": n_step, "us": t_step * 1e6, "gbps": gb(n_step * (row * 4 + 4), t_step)},
         "store_prefill_sized": {"tokens": n_big, "ms": t_big * 1e3, "gbps": gb(n_big * (row * 4 + 4), t_big)},
         "load": {"rows": rows, "ms": t_load * 1e3, "gbps": gb(rows * row * 4, t_load)},
@@ -249,6 +259,10 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     import diffulex_b200 as dlx
     from diffulex_b200 import dp, ops
+
+    if args.only_store_load:
+        print(json.dumps(store_load_bandwidth(dlx, dev, peaks()[0], args.store_load_seqs)))
+        return
 
     # ---- this rank's batch ----
     if args.scaling == "strong":
@@ -417,7 +431,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_store_load:
         del layers, graph, g_dec
         torch.cuda.empty_cache()
-        store_load = store_load_bandwidth(dlx, dev, peak)
+        store_load = store_load_bandwidth(dlx, dev, peak, args.store_load_seqs)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
