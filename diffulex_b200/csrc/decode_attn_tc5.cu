@@ -29,7 +29,8 @@
 // handing P to the tensor pipe in two halves of 64 keys; packing P to bf16 on the integer pipe; tracking the row
 // maximum inside the exponential loop; a second Q buffer at the price of a K stage; polling waits with nanosleep;
 // a separate short loop body for whole-tile copies; addressing a tail tile's rows directly instead of through the
-// row-pointer table; the tail tile as an item's third tile; programmatic dependent launch between the layer calls.
+// row-pointer table; the tail tile as an item's third tile; programmatic dependent launch between the layer calls;
+// L2 prefetch of the next item's Q and first K/V tiles by the (otherwise idle) epilogue warpgroup.
 //
 // Reference semantics: diffulex_kernel/python/dllm_flash_attn.py:163-347 and :632-637.
 #include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (resolved at run time, no libcuda link)
