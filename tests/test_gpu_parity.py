@@ -302,6 +302,20 @@ def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
     assert list(st) == [0, 0, 0, 0], f"a bounded wait expired: {list(st)}"
 
 
+def test_more_rounds_than_the_item_table_holds(dlx, monkeypatch):
+    """300 sequences x 32 KV heads = 9600 work items, i.e. 65 rounds on 148 persistent CTAs: one more than the
+    kernel's shared-memory item table holds, so the instantiation that decodes items per role is the one that
+    runs (the large configurations reach it only with forced key-range splits)."""
+    from diffulex_b200.workload import MASK_BD_FULL, make_problem, small_workload
+    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
+    rng = np.random.default_rng(5)
+    ctx = rng.integers(0, 200, size=300).tolist()
+    w = small_workload("many_items", 32, 32, 128, 32, 4, ctx, [4] * 300, MASK_BD_FULL, 41)
+    p = make_problem(w, device="cpu", values="numpy")
+    o = run_decode(dlx, to_dev(p), "static", 1)
+    torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)
+
+
 def test_out_of_range_scores_are_clamped_flagged_and_finite(dlx, monkeypatch):
     """A key whose score lies more than 100 log2-units above the softmax reference of its row (here ~130 nats
     above everything else) uses up the exponent headroom of the fixed-reference softmax: the kernel clamps
