@@ -959,10 +959,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 tc_fence_after();
                 const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
                 const uint32_t d = tmem + TM_S + b * 128;
+                // the 8 k-steps differ only in the start-address field of the two descriptors (16-byte units)
+                const uint64_t dq = smem_desc(sQ, 16, 1024), dk = smem_desc(kb, 16, 1024);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
-                    const uint32_t o = (ks >> 2) * REGION + (ks & 3) * 32;
-                    mma_ss(d, smem_desc(sQ + o, 16, 1024), smem_desc(kb + o, 16, 1024), ID_QK, ks > 0);
+                    constexpr uint32_t unit = 16;
+                    const uint64_t o = ((ks >> 2) * REGION + (ks & 3) * 32) / unit;
+                    mma_ss(d, dq + o, dk + o, ID_QK, ks > 0);
                 }
                 tc_commit(bar(B_SFULL + b));
                 DLX_TI(10, 3);
@@ -1004,9 +1007,10 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 tc_fence_after();
                 const uint32_t vb = sV + (idx % VSTAGES) * ITEM_BYTES;
                 const uint32_t pa = tmem + TM_P + b * 64;
+                const uint64_t dv = smem_desc(vb, REGION, 1024);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + TM_O, pa + kk * 8, smem_desc(vb + kk * 2048, REGION, 1024), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(tmem + TM_O, pa + kk * 8, dv + (uint64_t)(kk * 2048 / 16), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(bar(B_PFREE + b));
                 DLX_TI(0, 3);
                 tc_commit(bar(B_VEMPTY + idx % VSTAGES));
