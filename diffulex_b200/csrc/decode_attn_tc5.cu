@@ -395,7 +395,12 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // Round k of the item list goes to the CTAs in alternating direction (CTA 0..C-1, then C-1..0, ...): with the list
     // sorted longest-first this evens out the CTAs' totals, and the two row blocks of one (sequence, KV head),
     // neighbours in the list, still run at the same time on neighbouring CTAs and share their K/V through L2.
-    auto item_of_round = [&](int k) {
+    // With only a few rounds the 148 CTAs stay in lockstep and their item switches (bursts of row-wise copies) all fall
+    // into the same microsecond: neighbouring CTA pairs then walk their rounds from different starting points.  With
+    // many rounds they drift apart by themselves, and keeping every CTA's longest items first matters more for the tail.
+    const int rot = n_rounds <= 4 ? ((int)blockIdx.x >> 1) % max(n_rounds, 1) : 0;
+    auto item_of_round = [&](int k0) {
+        const int k = (k0 + rot) % max(n_rounds, 1);
         const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
         const int item = k * (int)gridDim.x + c;
         return item < items_total ? item : -1;
