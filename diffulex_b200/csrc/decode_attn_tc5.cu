@@ -55,10 +55,11 @@ constexpr int Q_BYTES = 2 * REGION;       // one Q tile, 2 head_dim halves
 constexpr int ITEM_BYTES = 2 * REGION;    // one K tile or one V tile
 #ifndef DLX_KSTAGES
 #define DLX_KSTAGES 2
-#define DLX_VSTAGES 3
+#define DLX_VSTAGES 2
 #endif
-// A ring slot is refilled when its tile has been consumed.  V is consumed late (P V follows the softmax), so it gets
-// the third stage; K is consumed by a Q K^T that already runs two tiles ahead of the softmax (two S buffers).
+// A ring slot is refilled when its tile has been consumed.  Two stages each, measured: one stage serialises copy and
+// MMA (+30 % run time), a third K or V stage is slower than two (more copies in flight at the item switches, where the
+// memory system is the contended resource).
 constexpr int KSTAGES = DLX_KSTAGES, VSTAGES = DLX_VSTAGES;
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
