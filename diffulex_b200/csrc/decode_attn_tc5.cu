@@ -27,7 +27,7 @@
 // Measured on B200 and rejected (each was slower than what is here): L2 prefetch of K/V tiles ahead of the rings,
 // by cp.async.bulk.prefetch.tensor or by prefetch.global.L2; fetching the next item's page ids or Q ahead of time;
 // handing P to the tensor pipe in two halves of 64 keys; packing P to bf16 on the integer pipe; tracking the row
-// maximum inside the exponential loop; a second Q buffer at the price of a K stage; polling waits with nanosleep;
+// maximum inside the exponential loop; a second Q buffer (fetched one item ahead); polling waits with nanosleep;
 // a separate short loop body for whole-tile copies; addressing a tail tile's rows directly instead of through the
 // row-pointer table; the tail tile as an item's third tile; programmatic dependent launch between the layer calls;
 // L2 prefetch of the next item's Q and first K/V tiles by the (otherwise idle) epilogue warpgroup.
