@@ -46,7 +46,7 @@ import torch
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch from the committed ncu captures
 # (profiles/), keyed by workload; None until a capture exists for that workload.
-NCU_TRAFFIC_BYTES = {"cfg2": 178767616 + 7958784}  # profiles/decode_attn_tc5_cfg2.md
+NCU_TRAFFIC_BYTES = {"cfg2": 178511104 + 9658112}  # profiles/decode_attn_tc5_cfg2.md
 
 
 def parse():
