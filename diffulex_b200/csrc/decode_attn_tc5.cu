@@ -399,7 +399,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // With only a few rounds the 148 CTAs stay in lockstep and their item switches (bursts of row-wise copies) all fall
     // into the same microsecond: neighbouring CTA pairs then walk their rounds from different starting points.  With
     // many rounds they drift apart by themselves, and keeping every CTA's longest items first matters more for the tail.
-    const int rot = n_rounds <= 4 ? ((int)blockIdx.x >> 1) % max(n_rounds, 1) : 0;
+    const int rot = n_rounds <= 8 ? ((int)blockIdx.x >> 1) % max(n_rounds, 1) : 0;
     auto item_of_round = [&](int k0) {
         const int k = (k0 + rot) % max(n_rounds, 1);
         const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
@@ -951,7 +951,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // S buffer and its use count
-                const int kq = k;
+                [[maybe_unused]] const int kq = k;   // read by the profile build's stamps
                 DLX_TI(10, 0);
                 if (u >= 1) {
                     ok = mbar_wait(bar(B_SFREE + b), (u - 1) & 1, abort_flag, 11, k);
@@ -1001,7 +1001,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // P buffer and its use count
-                const int kq = k;
+                [[maybe_unused]] const int kq = k;   // read by the profile build's stamps
                 DLX_TI(0, 0);
                 ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k);
                 DLX_TI(0, 1);
