@@ -31,7 +31,8 @@ class DecodeAttnParams(ctypes.Structure):
         ("struct_bytes", c_uint32), ("dtype", c_int32),
         ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
         ("out", c_void_p), ("block_tables", c_void_p), ("context_lens", c_void_p), ("cu_seqlens_q", c_void_p),
-        ("cu_seqlens_kv", c_void_p), ("seq_order", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_int64),
+        ("cu_seqlens_kv", c_void_p), ("schedule", c_void_p), ("schedule_bytes", c_int64),
+        ("workspace", c_void_p), ("workspace_bytes", c_int64),
         ("q_row_stride", c_int64), ("k_row_stride", c_int64), ("v_row_stride", c_int64), ("out_row_stride", c_int64),
         ("cache_page_stride", c_int64), ("cache_token_stride", c_int64), ("block_table_stride", c_int64),
         ("num_pages", c_int64),
@@ -56,10 +57,12 @@ _SIGNATURES = {
     "dlx_decode_attn_workspace_bytes": (c_int64, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn_num_splits": (c_int32, [ctypes.POINTER(DecodeAttnParams)]),
     "dlx_decode_attn": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
+    "dlx_decode_attn_schedule_bytes": (c_int64, [ctypes.POINTER(DecodeAttnParams)]),
+    "dlx_decode_attn_prepare": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p, c_int64, c_void_p]),
+    "dlx_stream_capture_id": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
     "dlx_static_scratch_bytes": (c_int64, []),
     "dlx_decode_attn_static_scratch": (c_int, [ctypes.POINTER(DecodeAttnParams), c_void_p]),
     "dlx_debug_device_status": (c_int, [ctypes.POINTER(c_int32)]),
-    "dlx_debug_profile": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

@@ -17,7 +17,8 @@ from pathlib import Path
 
 CSRC = Path(__file__).resolve().parent / "csrc"
 LIB = CSRC / "libdlx_b200.so"
-SOURCES = ["dlx_api.cu", "kv_cache_kernels.cu", "decode_attn_mma.cu", "decode_attn_tc5.cu"]
+SOURCES = ["dlx_api.cu", "kv_cache_kernels.cu", "decode_attn_mma.cu", "decode_attn_tc5.cu", "decode_attn_tc5_pair.cu",
+           "decode_sched.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",

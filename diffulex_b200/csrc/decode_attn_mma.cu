@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(C::NT, C::MINB) decode_attn_mma_kernel(const D
 
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / a.m_blocks, mb = blockIdx.y % a.m_blocks;
-    const int seq = a.seq_order ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
+    const int seq = (int)blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp % WM, wn = warp / WM;
     const int G = a.group;
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const DecodeArgs a)
     const int q0 = a.cu_q[seq];
     const int qn = a.cu_q[seq + 1] - q0;  // non-positive for padded sequences: nothing to merge
     const int64_t local = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (qn <= 0 || local >= (int64_t)qn * a.hq) return;
+    if (qn <= 0 || q0 < 0 || q0 + qn > a.total_q || local >= (int64_t)qn * a.hq) return;   // same guard as the main kernels
     const int64_t tok = q0 + local / a.hq, head = local % a.hq;
     if (tok >= a.total_q) return;
     const int64_t wid = tok * a.hq + head;

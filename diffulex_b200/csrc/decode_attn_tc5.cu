@@ -24,18 +24,9 @@
 // Every mbarrier wait is bounded; on expiry the CTA raises an abort word, everyone drains, the place is copied to a
 // device status word, TMEM is freed and the CTA returns (no trap, the context stays usable).
 //
-// Measured on B200 and rejected (each was slower than what is here): L2 prefetch of K/V tiles ahead of the rings,
-// by cp.async.bulk.prefetch.tensor or by prefetch.global.L2; fetching the next item's page ids or Q ahead of time;
-// handing P to the tensor pipe in two halves of 64 keys; packing P to bf16 on the integer pipe; tracking the row
-// maximum inside the exponential loop; a second Q buffer (fetched one item ahead); polling waits with nanosleep;
-// a separate short loop body for whole-tile copies; addressing a tail tile's rows directly instead of through the
-// row-pointer table; the tail tile as an item's third tile; programmatic dependent launch between the layer calls;
-// L2 prefetch of the next item's Q and first K/V tiles by the (otherwise idle) epilogue warpgroup.
-//
 // Reference semantics: diffulex_kernel/python/dllm_flash_attn.py:163-347 and :632-637.
 #include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (resolved at run time, no libcuda link)
 
-#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -43,6 +34,7 @@
 
 #include "dlx_common.cuh"
 #include "decode_attn.cuh"
+#include "tc5_common.cuh"
 
 namespace dlx {
 namespace tc5 {
@@ -74,15 +66,16 @@ constexpr int OFF_ROWMAP = OFF_STAGE + 4 * STAGE_WARP_BYTES;   // int2[128]: (ro
 constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;   // this CTA's decoded work items, one per round
 constexpr int MAX_ROUNDS = 64;                     // more rounds than this: every role decodes its items itself
 constexpr int ITEM_SLOT = 64;                      // bytes per decoded item
-constexpr int OFF_ARGS = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT;   // a copy of the argument block (256 bytes)
+constexpr int OFF_FLAGS = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT;  // one bit per round: the item has to be computed again, exactly
+constexpr int FLAG_WORDS = 128;                    // 4096 rounds; later rounds share the bits
+constexpr int OFF_ARGS = OFF_FLAGS + FLAG_WORDS * 4;   // a copy of the argument block (256 bytes)
 constexpr int SMEM_BYTES = OFF_ARGS + 256 + 1024;  // + slack for 1024-byte alignment
 static_assert(sizeof(DecodeArgs) <= 256, "argument block copy");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 // P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
-// precision however far later scores rise above m_ref, until 2^x leaves the bf16/fp32 range: a score more than
-// RAISE_LIMIT (in log2 units, ~69 nats) above the first tile's row maximum is clamped there and bit 1 of the
-// device status word is set.  Earlier keys then weigh < 2^-100 of the result, far below fp32 resolution.
-#define RAISE_LIMIT 100.f
+// precision however far later scores lie from m_ref, until 2^x leaves the bf16/fp32 range: an item in which a tile's
+// row sum of P exceeds DLX_SUM_HIGH, or whose final row sum falls below DLX_SUM_LOW although the row sees keys, is
+// flagged and computed again with a running maximum (tc5_common.cuh) before the CTA retires.
 constexpr int NUM_THREADS = 512;
 // Registers per thread after the roles split (the kernel starts with 65536 / 512 = 128 each): the four helper warps
 // and the epilogue warpgroup give registers back, the two softmax warpgroups (a row of 128 scores each) take them.
@@ -96,7 +89,6 @@ static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget
 constexpr int EPI_WARP0 = 12;
 constexpr int KLOAD_WARP = 8, VLOAD_WARP = 9, QK_WARP = 10, PV_WARP = 11;
 constexpr int NUM_LOADERS = 32;                    // lanes of one loader warp
-constexpr uint32_t WAIT_LIMIT = 1u << 21;
 // TMEM columns (512): two S buffers of 128 fp32 columns, two P buffers of 64 columns (128 bf16 keys), O
 constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
 
@@ -116,148 +108,15 @@ enum {
     B_MREMPTY = 26, // [slot] ... and have been read by the owner of the item's second tile
     B_LSFULL = 28,  // [slot] both warpgroups' partial row sums of an item are in shared memory (one use per item)
     B_LSEMPTY = 30, // [slot] ... and the epilogue warpgroup has read them
-    B_COUNT = 32
+    B_EPIDONE = 32, // the epilogue warpgroup has written its last output row (128 arrivals, once per launch)
+    B_COUNT = 33
 };
 
-__device__ int g_status[4];  // [0] bit 0: a bounded wait expired, bit 1: scores were clamped; [1] wait site, [2] tile, [3] CTA
-// Profile build (-DDLX_TC5_PROFILE=1) only: event times of CTA 0, in cycles since its start.  g_tl[round * 24 + event]
-// for rounds 0..4 (item-level events), rows 5..7 hold loader / issuer / softmax stamps of one mid-item tile;
-// g_cta_t holds every CTA's entry and exit time (globaltimer, ns).  Recording is switched on by the host
-// (dlx_debug_profile(1, ...)); the regular build compiles none of it.
-__device__ unsigned long long g_prof[24];   // legacy counters behind dlx_debug_profile's output argument (unused, zero)
-__device__ int g_prof_on;
-__device__ unsigned long long g_tl[8 * 24];
-__device__ unsigned long long g_cta_t[2 * 160];
-#ifndef DLX_TC5_PROFILE
-#define DLX_TC5_PROFILE 0
-#endif
+__device__ int g_status[4];  // [0] bit 0: a bounded wait expired; [1] wait site, [2] tile, [3] CTA
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n.reg .pred p;\n"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        "selp.b32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-// Bounded wait.  Returns false when the limit ran out or another thread of the CTA gave up.  Kept tiny, because it
-// is inlined at some forty sites (a called function cannot be used once the warps have resized their register
-// files): on expiry the site and tile go into the CTA's abort word, which one thread copies to the device status
-// word when the CTA retires.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int role, int tile) {
-    if (mbar_try(bar, parity)) return true;
-#pragma unroll 1
-    for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 255u) == 255u && *abort_flag) return false;
-    }
-    *abort_flag = 1 | ((tile & 0xffff) << 8) | (role << 24);
-    return false;
-}
 
-template <int N> __device__ __forceinline__ void reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
-template <int N> __device__ __forceinline__ void reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void fence_async_proxy() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-
-// The mbarrier gets one arrival (of its expected count) once every cp.async this thread issued so far has landed.
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
-}
-// Adds to the barrier's pending byte count without arriving.
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
-// One TMA box global -> shared, completion counted in bytes on `bar`.  Coordinates innermost first; c0 (elements of
-// 2 bytes) is 0 or 64, i.e. a multiple of 16 bytes as the copy engine requires.
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
-}
-
-// 64-bit shared-memory matrix descriptor, 128-byte swizzle, descriptor version 1.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)(lbo_bytes >> 4) << 16;
-    d |= (uint64_t)(sbo_bytes >> 4) << 32;
-    d |= 1ull << 46;
-    d |= 2ull << 61;
-    return d;
-}
-// kind::f16 instruction descriptor: fp32 accumulate, bf16 x bf16, M=128, N=128; b_mn: B is MN-major.
-__host__ __device__ constexpr uint32_t instr_desc(bool b_mn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
-}
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr) : "memory");
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
-}
-
-// One unit of work of a CTA: (sequence, KV head, block of 128 / group query tokens, key-range split), decoded from a
-// flat index.
+// One unit of work of a CTA: (sequence, KV head, block of 128 / group query tokens, key-range split), read from a
+// record of the launch's schedule (decode_sched.cu).
 struct alignas(8) Item {
     bool valid;        // has rows and at least one key tile
     bool empty_split;  // has rows but this split's key range is empty: only -inf log-sum-exps are written
@@ -268,50 +127,25 @@ struct alignas(8) Item {
     int t0, n;
 };
 
-__device__ __forceinline__ Item load_item(const DecodeArgs& a, int item) {
+__device__ __forceinline__ Item load_item(const DecodeArgs& a, const SchedRec* r) {
     Item it;
-    it.valid = false; it.empty_split = false;
-    it.seq = it.kvh = it.split = 0;
-    it.q0 = it.ctx = it.kv0 = it.nnew = it.total = it.row0 = it.rows_here = it.tok0 = it.cta_limit = it.full_until = it.t0 = it.n = 0;
-    if (item < 0) return it;
-    const int per_seq = a.hkv * a.m_blocks * a.num_splits;
-    const int z = item / per_seq, rem = item - z * per_seq;
-    const int y = rem / a.num_splits;
-    it.split = rem - y * a.num_splits;
-    it.kvh = y / a.m_blocks;
-    const int mb = y - it.kvh * a.m_blocks;
-    it.seq = a.seq_order ? a.seq_order[z] : z;
-    if (it.seq < 0 || it.seq >= a.num_seqs) return it;
-    it.q0 = a.cu_q[it.seq];
-    const int qn = a.cu_q[it.seq + 1] - it.q0;
-    if (qn <= 0 || it.q0 < 0 || it.q0 + qn > a.total_q) return it;
-    it.ctx = max(a.context_lens[it.seq], 0);
-    it.kv0 = it.q0; it.nnew = qn;
-    if (a.cu_kv != nullptr) {
-        it.kv0 = a.cu_kv[it.seq];
-        it.nnew = max(a.cu_kv[it.seq + 1] - it.kv0, 0);
-    }
+    const int4 w0 = *reinterpret_cast<const int4*>(&r->seq);
+    const int4 w1 = *reinterpret_cast<const int4*>(&r->q0);
+    const int4 w2 = *reinterpret_cast<const int4*>(&r->nnew);
+    it.seq = w0.x; it.kvh = w0.y; it.split = w0.w;
+    it.q0 = w1.x; it.ctx = w1.z; it.kv0 = w1.w;
+    it.nnew = w2.x; it.t0 = w2.y; it.n = w2.z;
+    it.valid = (w2.w & SCHED_VALID) != 0;
+    it.empty_split = (w2.w & SCHED_EMPTY_SPLIT) != 0;
     it.total = it.ctx + it.nnew;
     // A block holds q_tokens = 128 / group whole tokens (all `group` heads of each), so that its Q rows are one box
     // of the [token][head][head_dim] tensor; packed row r of the (sequence, KV head) is token r / group, head r % group.
-    const int tok0 = mb * a.q_tokens;
-    if (tok0 >= qn) return it;
-    it.row0 = tok0 * a.group;
-    it.tok0 = tok0;
-    it.rows_here = min(qn - tok0, a.q_tokens) * a.group;
-    it.cta_limit = it.full_until = it.total;
-    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) {
-        const int i_first = it.row0 / a.group, i_last = (it.row0 + it.rows_here - 1) / a.group;
-        it.cta_limit = it.ctx + min(it.nnew, (i_last / a.dbs + 1) * a.dbs);
-        it.full_until = it.ctx + min(it.nnew, (i_first / a.dbs + 1) * a.dbs);
-    }
-    const int n_tiles = (it.cta_limit + TILE_N - 1) / TILE_N;
-    const int tiles_per_split = (n_tiles + a.num_splits - 1) / a.num_splits;
-    it.t0 = it.split * tiles_per_split;
-    const int t1 = min(n_tiles, it.t0 + tiles_per_split);
-    if (it.t0 >= t1) { it.empty_split = true; return it; }
-    it.n = t1 - it.t0;
-    it.valid = true;
+    it.tok0 = w0.z * a.q_tokens;
+    it.row0 = it.tok0 * a.group;
+    it.rows_here = max(min(w1.y - it.tok0, a.q_tokens), 0) * a.group;
+    it.cta_limit = r->limit;
+    it.full_until = it.total;
+    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) it.full_until = it.ctx + min(it.nnew, (it.tok0 / a.dbs + 1) * a.dbs);
     return it;
 }
 
@@ -331,29 +165,11 @@ struct TmaMaps {
 // Persistent kernel: one CTA per SM walks its rounds of the (longest-first) item list.  Every role keeps running
 // counters for the rings and buffers, so the pipeline never drains between items: while the softmax warpgroups
 // finish item i the loaders already fetch K / V of item i + 1 and the Q K^T issuer fills its first two S buffers.
-// TABLE: the CTA's rounds fit the shared-memory item table (the usual case); otherwise every role decodes its items
-// itself, at the price of five inlined copies of the decoder, which is why that is a separate instantiation.
-template <bool TABLE>
+// The CTA's first MAX_ROUNDS records are decoded once into a shared-memory table; later rounds (rare) are decoded from
+// the global records by every role.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps maps) {
     extern __shared__ unsigned char smem_raw[];
-    // Event stamps of the profile build (cycles since CTA 0 started): DLX_TL0 set-up events, DLX_TL item-level events
-    // of round `round`, DLX_TT / DLX_TI softmax / issuer events of tiles 40 and 41 of an item.  Empty otherwise.
-#if DLX_TC5_PROFILE
-    const long long t_entry = clock64();
-    const bool tl_on = g_prof_on && blockIdx.x == 0;
-    if (g_prof_on && threadIdx.x == 0 && blockIdx.x < 160) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_cta_t[blockIdx.x] = t; }
-#define DLX_STAMP_AT(idx) g_tl[(idx)] = (unsigned long long)(clock64() - t_entry)
-#define DLX_TL0(ev) do { if (tl_on) DLX_STAMP_AT(ev); } while (0)
-#define DLX_TL(ev) do { if (tl_on && round < 5) DLX_STAMP_AT(round * 24 + (ev)); } while (0)
-#define DLX_TI(base, k) do { if (tl_on && (kq == 40 || kq == 41)) DLX_STAMP_AT(6 * 24 + (base) + (kq - 40) * 5 + (k)); } while (0)
-#define DLX_TT(k) do { if (tl_on && (jj == 40 || jj == 41) && L == 0) DLX_STAMP_AT(7 * 24 + w * 12 + (k)); } while (0)
-#else
-#define DLX_TL0(ev) do { } while (0)
-#define DLX_TL(ev) do { } while (0)
-#define DLX_TI(base, k) do { } while (0)
-#define DLX_TT(k) do { } while (0)
-#endif
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -384,6 +200,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         }
         mbar_init(bar(B_OFULL), 1);
         mbar_init(bar(B_OFREE), 128);
+        mbar_init(bar(B_EPIDONE), 128);
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(B_MRFULL + s), 128); mbar_init(bar(B_MREMPTY + s), 128);
             mbar_init(bar(B_LSFULL + s), 256); mbar_init(bar(B_LSEMPTY + s), 128);
@@ -391,34 +208,19 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    const int items_total = a_param.items_total;
-    const int n_rounds = (items_total + (int)gridDim.x - 1) / (int)gridDim.x;
-    // Round k of the item list goes to the CTAs in alternating direction (CTA 0..C-1, then C-1..0, ...): with the list
-    // sorted longest-first this evens out the CTAs' totals, and the two row blocks of one (sequence, KV head),
-    // neighbours in the list, still run at the same time on neighbouring CTAs and share their K/V through L2.
-    // With only a few rounds the 148 CTAs stay in lockstep and their item switches (bursts of row-wise copies) all fall
-    // into the same microsecond: neighbouring CTA pairs then walk their rounds from different starting points.  With
-    // many rounds they drift apart by themselves, and keeping every CTA's longest items first matters more for the tail.
-    const int rot = n_rounds <= 8 ? ((int)blockIdx.x >> 1) % max(n_rounds, 1) : 0;
-    auto item_of_round = [&](int k0) {
-        const int k = (k0 + rot) % max(n_rounds, 1);
-        const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
-        const int item = k * (int)gridDim.x + c;
-        return item < items_total ? item : -1;
-    };
-    // All rounds are decoded up front, one thread per round: the chain of dependent metadata loads (sequence order ->
-    // lengths -> offsets, ~2 us) is paid once per CTA instead of once per item and role.
+    // This CTA's records: placed by the schedule kernel (longest-processing-time greedy, longest item first).
+    const int rec0 = a_param.sched_off[blockIdx.x];
+    const int n_rounds = a_param.sched_off[blockIdx.x + 1] - rec0;
+    const SchedRec* recs_g = a_param.sched_recs + rec0;
     Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
-    if (TABLE && tid < n_rounds) items_s[tid] = load_item(a_param, item_of_round(tid));
-    if (tid == 0) DLX_TL0(22);
+    if (tid < min(n_rounds, MAX_ROUNDS)) items_s[tid] = load_item(a_param, recs_g + tid);
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
     int2* rowmap = reinterpret_cast<int2*>(gbase + OFF_ROWMAP);
     if (tid >= 128 && tid < 256) rowmap[tid - 128] = make_int2((tid - 128) / G, (tid - 128) % G);
-    auto get_item = [&](int k) {
-        if constexpr (TABLE) return items_s[k];
-        else return load_item(a, item_of_round(k));
-    };
+    uint32_t* redo_flags = reinterpret_cast<uint32_t*>(gbase + OFF_FLAGS);
+    if (tid >= 256 && tid < 256 + FLAG_WORDS) redo_flags[tid - 256] = 0;
+    auto get_item = [&](int k) { return k < MAX_ROUNDS ? items_s[k] : load_item(a, recs_g + k); };
     {
         // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
         // by a Q box: zero them once, so that the unused TMEM lanes only ever see finite scores.
@@ -438,7 +240,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // own decode of the item): otherwise this third dependent load would start only after the set-up barrier.
     bool bt_preloaded = false;
     if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
-        const Item f = load_item(a_param, item_of_round(0));
+        Item f; f.valid = false;
+        if (n_rounds > 0) f = load_item(a_param, recs_g);
         if (f.valid) {
             const int pages = min((f.ctx + a_param.page_size - 1) / a_param.page_size, a_param.max_blocks);
             if (pages <= BT_SLOTS) {
@@ -457,7 +260,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (tid == 0) DLX_TL0(23);
     // Running totals over the valid items this CTA has finished (identical in every role):
     //   done = items, ck = key tiles.  Tile k of an item has running index ck + k: S/P buffer (ck + k) & 1, and
     //   (ck + k) >> 1 earlier uses of that buffer.
@@ -470,8 +272,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         // items: the tile with running index g belongs to warpgroup g & 1, which always works on S buffer / P buffer
         // g & 1.  One warp per SM sub-partition cannot issue fast enough to keep the MUFU unit busy; two can, and
         // while one waits for its S the other works.  Both scale their P by the SAME per-row reference m_ref = scaled
-        // row maximum of the item's first tile (a fixed reference is exact as long as exponents stay in range: see
-        // RAISE_LIMIT), so their outputs add up in the one O accumulator and their row sums add up at the end.
+        // row maximum of the item's first tile (a fixed reference is exact as long as exponents stay in range; items
+        // that leave it are recomputed), so their outputs add up in the one O accumulator and their row sums add up at the end.
         // Neither waits for an item's output to be written: that is the epilogue warpgroup's job.
         const int w = warp >> 2;                       // warpgroup = parity of the running tile index
         const int L = tid & 127;                       // TMEM lane == row inside the tile
@@ -484,7 +286,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         bool alive = true;
 #pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
-            if (L == 0) DLX_TL(w ? 20 : 19);
             const Item it = get_item(round);
             const int64_t head0 = (int64_t)it.kvh * G;
             if (it.empty_split) {
@@ -507,16 +308,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             int limit = it.total;
             if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL && row_valid) limit = it.ctx + min(it.nnew, ((it.tok0 + my_row.x) / a.dbs + 1) * a.dbs);
             float m_ref = 0.f, l_run = 0.f;
-            if (tid == 0) DLX_TL(0);
+            bool out_of_range = false;
 #pragma unroll 1
             for (int jj = jj_first; jj < n && alive; jj += 2) {
                 const int u = (ck + jj) >> 1;              // use count of this warpgroup's buffers: phase of their barriers
-                DLX_TT(0);
                 bool ok = mbar_wait(bar(B_SFULL + w), u & 1, abort_flag, 1 + w, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
-                DLX_TT(1);
-                if (jj == jj_first && L == 0) DLX_TL(w ? 6 : 1);
                 // Ring bookkeeping of the row reference (all warps, valid rows or not, keep the barrier counts whole):
                 // the owner of tile 0 fills the slot, the owner of tile 1 drains it.
                 if (multi && jj == 0 && mr >= 2) {
@@ -550,20 +348,19 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     tmem_ld_wait();
                     tc_fence_before();
                     mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
-                    DLX_TT(2);
-                    float mx4[4];  // four independent chains: the max is latency-, not issue-bound
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        mx4[c] = -INFINITY;
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2)
-                            mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
-                    }
-                    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
                     if (jj == 0) {
-                        // First tile: fix the reference.  A row that sees none of this tile's keys (block-causal rows of
-                        // an early block; the first tile is a late key tile) takes the maximum over the tile's hidden
-                        // keys instead: same sequence, same magnitude of scores.  0 for a padding row.
+                        // First tile: its row maximum fixes the reference (later tiles compute no maximum at all).  A row
+                        // that sees none of this tile's keys (block-causal rows of an early block; the first tile is a
+                        // late key tile) takes the maximum over the tile's hidden keys instead.  0 for a padding row.
+                        float mx4[4];  // four independent chains: the max is latency-, not issue-bound
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            mx4[c] = -INFINITY;
+#pragma unroll
+                            for (int e = 0; e < 32; e += 2)
+                                mx4[c] = max3(mx4[c], __uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1]));
+                        }
+                        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
                         m_ref = (mx != -INFINITY) ? mx : (mx_any != -INFINITY ? mx_any * sl2 : 0.f);
                         if (multi) {
                             xm[slot * 128 + L] = m_ref;
@@ -575,17 +372,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         m_ref = xm[slot * 128 + L];
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    if (__any_sync(0xffffffffu, mx - m_ref > RAISE_LIMIT)) {
-                        // Exponent headroom used up (see RAISE_LIMIT): clamp the offending scores (in registers) and flag
-                        // it in the device status word.  Rare.
-                        atomicOr(&g_status[0], 2);
-                        const float cap = (m_ref + RAISE_LIMIT) / sl2;
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) v[c][e] = __float_as_uint(fminf(__uint_as_float(v[c][e]), cap));
-                    }
-                    DLX_TT(3);
                     if (u >= 1) {
                         // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
                         // this buffer must have been consumed before the next one goes in (and before this barrier's
@@ -593,7 +379,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
                         if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
                     }
-                    DLX_TT(4);
                     // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
@@ -610,10 +395,10 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         tmem_st16(tP + c * 16, pk);
                     }
                     lacc0 = __fadd2_rn(lacc0, lacc1);
-                    l_run += lacc0.x + lacc0.y;
-                    DLX_TT(5);
+                    const float tsum = lacc0.x + lacc0.y;
+                    out_of_range |= !(tsum <= DLX_SUM_HIGH);   // exponent range left (also catches NaN): redo the item
+                    l_run += tsum;
                     tmem_st_wait();
-                    DLX_TT(6);
                 } else {
                     // A warp without valid rows only keeps the barrier counts whole.  It must not run ahead either: its
                     // arrival for a later tile landing in the phase of this one would complete that phase early.
@@ -632,8 +417,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 tc_fence_before();
                 mbar_arrive(bar(B_PFULL + w));
             }
-            if (L == 0) DLX_TL(w ? 7 : 2);
             if (!alive) break;
+            if (__any_sync(0xffffffffu, out_of_range && row_valid) && lane == 0)
+                atomicOr(&redo_flags[(round >> 5) & (FLAG_WORDS - 1)], 1u << (round & 31));
             // ---- hand the item over to the epilogue warpgroup: partial row sums (and the reference) through a ring of
             // two slots, one use per item.  A warpgroup without a tile in the item (one-tile items) hands over a zero.
             {
@@ -646,8 +432,29 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 if (jj_first == 0) xs[ls * 384 + 256 + L] = m_ref;   // the owner of tile 0 set it
                 mbar_arrive(bar(B_LSFULL + ls));
             }
-            if (tid == 0) DLX_TL(3);
             ++done; ck += n; mr += multi ? 1 : 0;
+        }
+        // ---- items that left the fixed reference's range: their rows again, exactly ----
+        // The epilogue warpgroup signals its last output row (and its last flag); by then every
+        // MMA has completed (its last O_full), so the K / V rings are idle and serve as scratch.
+        const bool epi_done = mbar_wait(bar(B_EPIDONE), 0, abort_flag, 15, -7);
+        if (alive && epi_done && *abort_flag == 0) {
+            float* scratch = reinterpret_cast<float*>(gbase + OFF_K);
+            static_assert(8 * (REDO_CHUNK + HD) * 4 <= (KSTAGES + VSTAGES) * ITEM_BYTES, "redo scratch");
+#pragma unroll 1
+            const int flag_words = min((n_rounds + 31) >> 5, FLAG_WORDS);
+#pragma unroll 1
+            for (int wd = 0; wd < flag_words; ++wd) {
+                uint32_t bits = redo_flags[wd];
+                while (bits) {
+                    const int b = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    for (int round = wd * 32 + b; round < n_rounds; round += 32 * FLAG_WORDS) {
+                        const Item it = get_item(round);
+                        if (it.valid && it.rows_here > 0) redo_item_exact(a, it, warp, lane, scratch);
+                    }
+                }
+            }
         }
     } else if (warp >= EPI_WARP0) {
         // =========================== epilogue warpgroup: O / l -> global ===========================
@@ -671,12 +478,20 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             mbar_arrive(bar(B_LSEMPTY + ls));
             ok = mbar_wait(bar(B_OFULL), done & 1, abort_flag, 3, it.n);
             if (!__all_sync(0xffffffffu, ok)) break;
-            if (L == 0) DLX_TL(4);
             tc_fence_after();
             const int rows_here = it.rows_here;
             const int head0 = it.kvh * G;
             const bool row_valid = L < rows_here;
             if (wq * 32 < rows_here) {
+                // a row that sees at least one key of this range must have a row sum well inside fp32's range
+                bool low = false;
+                if (row_valid && !(l_run >= DLX_SUM_LOW)) {
+                    int limit = it.total;
+                    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) limit = it.ctx + min(it.nnew, ((it.tok0 + rowmap[L].x) / a.dbs + 1) * a.dbs);
+                    low = limit > it.t0 * TILE_N;
+                }
+                if (__any_sync(0xffffffffu, low) && lane == 0)
+                    atomicOr(&redo_flags[(round >> 5) & (FLAG_WORDS - 1)], 1u << (round & 31));
                 const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
                 if (a.num_splits == 1) {
                     // bf16 output, 64 head_dim columns (128 bytes of each row) per pass.  A thread holds one ROW, so direct
@@ -691,7 +506,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         if (c == 1) {
                             tc_fence_before();
                             mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite it
-                            if (L == 0) DLX_TL(17);
                         }
 #pragma unroll
                         for (int q4 = 0; q4 < 8; ++q4) {
@@ -743,9 +557,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             } else {
                 mbar_arrive(bar(B_OFREE));
             }
-            if (L == 0) DLX_TL(5);
             ++done;
         }
+        mbar_arrive(bar(B_EPIDONE));   // (release: output rows and flags are written)
     } else {
     reg_dec<HELPER_REGS>();   // one site for the whole helper warpgroup (warps 8..11)
     if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
@@ -857,15 +671,8 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 const CUtensorMap* lvl_maps = which ? maps.v : maps.k;
                 const bool one_box = by_tma && a.tma_box_rows == TILE_N;   // the tile is one box (pair) of one page
                 const int pid0 = (one_box && pj < a.max_blocks) ? bt[pj] : -1;   // a bad id is out of bounds: zero fill
-#if DLX_TC5_PROFILE
-                if (tl_on && jj == 40 && lane == 0) g_tl[5 * 24 + which * 6 + 0] = (unsigned long long)(clock64() - t_entry);
-#endif
                 bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-#if DLX_TC5_PROFILE
-                if (tl_on && jj == 40 && lane == 0) g_tl[5 * 24 + which * 6 + 1] = (unsigned long long)(clock64() - t_entry);
-#endif
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                if (jj == 0 && lane == 0) DLX_TL(14 + which);
                 if (one_box) {
                     if (lane == 0) {
                         mbar_arrive_expect_tx(full, ITEM_BYTES);
@@ -895,14 +702,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         mbar_arrive(full);
                     }
                 }
-#if DLX_TC5_PROFILE
-                if (tl_on && jj == 40 && lane == 0) {   // when did the copy land?  (polls the full barrier: profile build only)
-                    g_tl[5 * 24 + which * 6 + 2] = (unsigned long long)(clock64() - t_entry);
-                    const uint32_t par_full = (idx / stages) & 1;
-                    for (int spin = 0; spin < 100000 && !mbar_try(full, par_full); ++spin) { }
-                    g_tl[5 * 24 + which * 6 + 3] = (unsigned long long)(clock64() - t_entry);
-                }
-#endif
                 if (!by_tma) {
                     const uint32_t dbase = d0 + half_off;
                     const int pairs = (c_end - tma_rows + 1) >> 1;
@@ -940,27 +739,21 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 // sequence are loaded but their rows are never stored.
                 if (done > 0) ok = mbar_wait(bar(B_QEMPTY), (done - 1) & 1, abort_flag, 6, -2);
                 if (!ok) break;
-                DLX_TL(8);
                 mbar_arrive_expect_tx(bar(B_QFULL), 2u * (uint32_t)(a.q_tokens * G) * 128u);
                 tma_load_3d(sQ, &maps.q, 0, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
                 tma_load_3d(sQ + REGION, &maps.q, 64, it.kvh * G, it.q0 + it.tok0, bar(B_QFULL));
             }
             ok = mbar_wait(bar(B_QFULL), done & 1, abort_flag, 7, -1);
-            DLX_TL(9);
 #pragma unroll 1
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // S buffer and its use count
-                [[maybe_unused]] const int kq = k;   // read by the profile build's stamps
-                DLX_TI(10, 0);
                 if (u >= 1) {
                     ok = mbar_wait(bar(B_SFREE + b), (u - 1) & 1, abort_flag, 11, k);
                     if (!ok) break;
                 }
-                DLX_TI(10, 1);
                 ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
                 if (!ok) break;
-                DLX_TI(10, 2);
                 fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
                 tc_fence_after();
                 const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
@@ -974,11 +767,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     mma_ss(d, dq + o, dk + o, ID_QK, ks > 0);
                 }
                 tc_commit(bar(B_SFULL + b));
-                DLX_TI(10, 3);
                 tc_commit(bar(B_KEMPTY + idx % KSTAGES));
             }
             if (ok) tc_commit(bar(B_QEMPTY));   // every Q K^T of this item has read Q
-            DLX_TL(10);
             ++done; ck += n;
         }
       }
@@ -996,19 +787,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             if (!it.valid) continue;
             const int n = it.n;
             if (done > 0) ok = mbar_wait(bar(B_OFREE), (done - 1) & 1, abort_flag, 8, -2);  // the epilogue has read O
-            DLX_TL(11);
 #pragma unroll 1
             for (int k = 0; k < n && ok; ++k) {
                 const int idx = ck + k;
                 const int b = idx & 1, u = idx >> 1;   // P buffer and its use count
-                [[maybe_unused]] const int kq = k;   // read by the profile build's stamps
-                DLX_TI(0, 0);
                 ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k);
-                DLX_TI(0, 1);
                 ok = ok && mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                 if (!ok) break;
-                DLX_TI(0, 2);
-                if (k == 0) DLX_TL(12);
                 fence_async_proxy();
                 tc_fence_after();
                 const uint32_t vb = sV + (idx % VSTAGES) * ITEM_BYTES;
@@ -1018,11 +803,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + TM_O, pa + kk * 8, dv + (uint64_t)(kk * 2048 / 16), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(bar(B_PFREE + b));
-                DLX_TI(0, 3);
                 tc_commit(bar(B_VEMPTY + idx % VSTAGES));
             }
             if (ok) tc_commit(bar(B_OFULL));
-            DLX_TL(13);
             ++done; ck += n;
         }
       }
@@ -1031,9 +814,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     // ---- teardown: everyone arrives (all waits above are bounded), then TMEM is returned ----
     tc_fence_before();
     __syncthreads();
-#if DLX_TC5_PROFILE
-    if (g_prof_on && tid == 0 && blockIdx.x < 160) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_cta_t[160 + blockIdx.x] = t; }
-#endif
     if (tid == 0 && *abort_flag != 0) {   // a wait ran out: record where (the first CTA to report wins)
         const int word = *abort_flag;
         if (atomicCAS(&g_status[0], 0, 1) == 0) {
@@ -1109,15 +889,21 @@ int cache_map(const MapKey& k, CUtensorMap* out) {
 }
 }  // namespace
 
+namespace tc5 {
+int tc5_cache_map(const void* ptr, int64_t page_stride, int64_t token_stride, int64_t num_pages, int hkv, int page_size,
+                  int rows, int rank, CUtensorMap* out) {
+    MapKey k{ptr, page_stride, token_stride, num_pages, hkv, page_size, rows, rank};
+    return cache_map(k, out);
+}
+}  // namespace tc5
+
 int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     static bool attr_done[16] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 16 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              tc5::SMEM_BYTES);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(tc5::decode_attn_tc5_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc5::SMEM_BYTES);
         if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "cudaFuncSetAttribute(tc5 smem=%d): %s", tc5::SMEM_BYTES, cudaGetErrorString(e));
         attr_done[dev] = true;
     }
@@ -1132,7 +918,7 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     const bool fits = a.max_blocks > 0 && a.num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
     const bool strides_ok = a.token_stride * 2 % 16 == 0 && a.page_stride * 2 % 16 == 0 &&
                             a.page_stride * 2 < (1ll << 40) && a.num_pages < (1ll << 31);
-    if (fits && strides_ok && getenv("DLX_TC5_NO_TMA") == nullptr) {
+    if (fits && strides_ok) {
         const int rows = ps < 128 ? ps : 128;
         int lvl0 = 0;
         while ((128 >> lvl0) > rows) ++lvl0;
@@ -1149,29 +935,15 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     // Q blocks of 128 / group whole tokens: one box {64, group, tokens} per head_dim half
     a.q_tokens = 128 / a.group;
     a.q_by_tma = 0;
-    if (a.total_q > 0 && a.q_rs * 2 % 16 == 0 && a.q_rs * 2 < (1ll << 40) && getenv("DLX_TC5_NO_TMA") == nullptr) {
+    if (a.total_q > 0 && a.q_rs * 2 % 16 == 0 && a.q_rs * 2 < (1ll << 40)) {
         MapKey kq{a.q, a.q_rs, 0, a.total_q, a.hq, a.group, a.q_tokens, 3};
         const int rc = cache_map(kq, &maps.q);
         if (rc != DLX_OK) return rc;
         a.q_by_tma = 1;
     }
-    // Persistent CTAs: one per SM (fewer when there is less work), each walks its share of the item list.
-    static int sm_count[16] = {};
-    int sms = dev < 16 ? sm_count[dev] : 0;
-    if (sms == 0) {
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-        if (dev < 16) sm_count[dev] = sms;
-    }
-    const int64_t items = (int64_t)a.num_seqs * a.hkv * a.m_blocks * a.num_splits;
-    if (items > (1ll << 30)) return fail(DLX_ERR_UNSUPPORTED, "decode: too many work items");
-    a.items_total = (int)items;
-    if (const char* g = getenv("DLX_TC5_GRID")) sms = atoi(g) > 0 ? atoi(g) : sms;
-    dim3 grid((unsigned)(items < sms ? items : sms)), block(tc5::NUM_THREADS);
-    const int64_t rounds = (items + grid.x - 1) / grid.x;
-    if (rounds <= tc5::MAX_ROUNDS && rounds <= tc5::NUM_THREADS)
-        tc5::decode_attn_tc5_kernel<true><<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
-    else
-        tc5::decode_attn_tc5_kernel<false><<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
+    // Persistent CTAs: one per bin of the schedule (one per SM, fewer when there is less work).
+    dim3 grid((unsigned)a.bins), block(tc5::NUM_THREADS);
+    tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
     return check_launch("decode_attn_tc5_kernel");
 }
 
@@ -1184,24 +956,5 @@ int read_tc5_status(int out[4]) {
     return DLX_OK;
 }
 
-#if DLX_TC5_PROFILE
-extern "C" int dlx_debug_timeline(unsigned long long* out) {   // profile build only: copies out and clears [8][16] event times
-    cudaError_t e = cudaMemcpyFromSymbol(out, tc5::g_tl, sizeof(unsigned long long) * 192);
-    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(out + 192, tc5::g_cta_t, sizeof(unsigned long long) * 320);
-    unsigned long long zero[192] = {};
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_tl, zero, sizeof(zero));
-    return e == cudaSuccess ? DLX_OK : DLX_ERR_CUDA;
-}
-#endif
-
-int tc5_profile(int enable, unsigned long long out[24]) {
-    cudaError_t e = cudaSuccess;
-    if (out != nullptr) e = cudaMemcpyFromSymbol(out, tc5::g_prof, sizeof(unsigned long long) * 24);
-    unsigned long long zero[24] = {};
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof, zero, sizeof(zero));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tc5::g_prof_on, &enable, sizeof(int));
-    if (e != cudaSuccess) return fail(DLX_ERR_CUDA, "tc5_profile: %s", cudaGetErrorString(e));
-    return DLX_OK;
-}
 
 }  // namespace dlx

@@ -1,0 +1,231 @@
+// Device-side schedule of one decode-attention launch of the persistent tcgen05 kernels.
+//
+// One small kernel turns the per-step metadata (context_lens, cu_seqlens, block tables: what the reference's model
+// runner fills on the host, diffulex/strategy/block_diffusion/engine/model_runner.py:125-158) into packed work-item
+// records: every (sequence, KV head, query-token block, key-range split) with its lengths and offsets resolved and
+// the ids of its last pages attached, assigned to the persistent CTAs (bins) by a longest-processing-time greedy
+// over the items sorted by key-tile count.  It runs once per metadata state (all layers of a step share it), on the
+// stream, with no host involvement, so a captured step re-plans itself when its static buffers are refilled.
+#include "dlx_common.cuh"
+#include "decode_attn.cuh"
+
+namespace dlx {
+
+namespace {
+
+constexpr int SORT_MAX = 4096;      // items sorted and placed greedily; larger launches are dealt round-robin
+constexpr int SCHED_THREADS = 1024;
+constexpr int TILE_N = 128;
+
+struct ItemShape {
+    int seq, kvh, mb, split;
+    int q0, qn, ctx, kv0, nnew, t0, n, flags, limit;
+};
+
+// Everything about work item `item` that follows from the metadata.  flags == 0: the item has no query rows (a
+// token block past the end of a short sequence, a padded sequence): it gets no record.
+__device__ ItemShape item_shape(const DecodeArgs& a, int item) {
+    ItemShape it{};
+    const int per_seq = a.hkv * a.m_blocks * a.num_splits;
+    it.seq = item / per_seq;
+    const int rem = item - it.seq * per_seq;
+    const int y = rem / a.num_splits;
+    it.split = rem - y * a.num_splits;
+    it.kvh = y / a.m_blocks;
+    it.mb = y - it.kvh * a.m_blocks;
+    if (it.seq >= a.num_seqs) return it;
+    it.q0 = a.cu_q[it.seq];
+    it.qn = a.cu_q[it.seq + 1] - it.q0;
+    if (it.qn <= 0 || it.q0 < 0 || it.q0 + it.qn > a.total_q) return it;
+    it.ctx = max(a.context_lens[it.seq], 0);
+    it.kv0 = it.q0; it.nnew = it.qn;
+    if (a.cu_kv != nullptr) {
+        it.kv0 = a.cu_kv[it.seq];
+        it.nnew = max(a.cu_kv[it.seq + 1] - it.kv0, 0);
+    }
+    const int tok0 = it.mb * a.tokens_per_item;
+    if (tok0 >= it.qn) return it;
+    const int tok_last = min(it.qn, tok0 + a.tokens_per_item) - 1;
+    it.limit = it.ctx + it.nnew;
+    if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) it.limit = it.ctx + min(it.nnew, (tok_last / a.dbs + 1) * a.dbs);
+    const int n_tiles = (it.limit + TILE_N - 1) / TILE_N;
+    const int per_split = (n_tiles + a.num_splits - 1) / a.num_splits;
+    it.t0 = it.split * per_split;
+    const int t1 = min(n_tiles, it.t0 + per_split);
+    if (it.t0 >= t1) { it.flags = SCHED_EMPTY_SPLIT; it.n = 0; return it; }
+    it.n = t1 - it.t0;
+    it.flags = SCHED_VALID;
+    return it;
+}
+
+__device__ void write_record(const DecodeArgs& a, const ItemShape& it, SchedRec* out) {
+    SchedRec r;
+    r.seq = it.seq; r.kvh = it.kvh; r.mb = it.mb; r.split = it.split;
+    r.q0 = it.q0; r.qn = it.qn; r.ctx = it.ctx; r.kv0 = it.kv0;
+    r.nnew = it.nnew; r.t0 = it.t0; r.n = it.n; r.flags = it.flags;
+    r.limit = it.limit; r.reserved = 0;
+    r.first_page = 0; r.n_pages = 0;
+#pragma unroll
+    for (int j = 0; j < kSchedPages; ++j) r.pages[j] = -1;
+    if ((it.flags & SCHED_VALID) && a.max_blocks > 0 && it.ctx > 0) {
+        const int last_key = min((it.t0 + it.n) * TILE_N, it.ctx) - 1;   // last cached key of the range
+        if (last_key >= it.t0 * TILE_N) {
+            const int last_page = min(last_key / a.page_size, a.max_blocks - 1);
+            r.first_page = max(0, last_page - (kSchedPages - 1));
+            r.n_pages = last_page - r.first_page + 1;
+            const int32_t* bt = a.block_tables + (int64_t)it.seq * a.bt_stride;
+            for (int j = 0; j < r.n_pages; ++j) r.pages[j] = bt[r.first_page + j];
+        }
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(&r);
+    uint4* dst = reinterpret_cast<uint4*>(out);
+#pragma unroll
+    for (int j = 0; j < (int)(sizeof(SchedRec) / 16); ++j) dst[j] = src[j];
+}
+
+// cost of an item for the placement: its key tiles plus one tile's worth of per-item overhead
+__device__ __forceinline__ uint32_t item_cost(const ItemShape& it) {
+    return it.flags == 0 ? 0u : (uint32_t)it.n + 1u;
+}
+
+__global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const DecodeArgs a) {
+    // (~cost << 32) | item: ascending = longest first, ties by index.  The placement overwrites the upper half with
+    // bin << 16 | position inside the bin.
+    __shared__ unsigned long long keys[SORT_MAX];
+    __shared__ int offs[kSchedMaxBins + 1];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int n_items = a.items_total, bins = a.bins;
+    int32_t* off_out = const_cast<int32_t*>(a.sched_off);
+    SchedRec* recs = const_cast<SchedRec*>(a.sched_recs);
+
+    if (n_items > SORT_MAX) {
+        // Too many items to sort in shared memory: deal them round-robin in natural order (every item gets a
+        // record, rows or not; kernels skip records without the VALID / EMPTY_SPLIT bits).
+        for (int b = tid; b <= bins; b += SCHED_THREADS) {
+            // bin b holds items b, b + bins, ...: offsets are the running counts
+            int64_t before = 0;
+            if (b > 0) {
+                const int full = n_items / bins, extra = n_items % bins;
+                before = (int64_t)full * b + min(b, extra);
+            }
+            off_out[b] = (int)before;
+        }
+        for (int i = tid; i < n_items; i += SCHED_THREADS) {
+            const int b = i % bins, pos = i / bins;
+            const int full = n_items / bins, extra = n_items % bins;
+            const int64_t base = (int64_t)full * b + min(b, extra);
+            write_record(a, item_shape(a, i), recs + base + pos);
+        }
+        return;
+    }
+
+    int n_pad = 1;
+    while (n_pad < n_items) n_pad <<= 1;
+    for (int i = tid; i < n_pad; i += SCHED_THREADS) {
+        unsigned long long key = ~0ull;
+        if (i < n_items) {
+            const uint32_t c = item_cost(item_shape(a, i));
+            key = ((unsigned long long)(0xffffffffu - c) << 32) | (uint32_t)i;
+        }
+        keys[i] = key;
+    }
+    __syncthreads();
+    // bitonic sort, ascending
+    for (int k = 2; k <= n_pad; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < n_pad; i += SCHED_THREADS) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = keys[i], y = keys[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((x > y) == up) { keys[i] = y; keys[ixj] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // Longest-processing-time greedy by one warp: every lane keeps the loads of bins lane, lane + 32, ...; per item
+    // a warp-wide minimum finds the least loaded bin (lowest index on ties), whose lane takes the item.
+    if (tid < 32) {
+        constexpr int PER_LANE = kSchedMaxBins / 32;
+        uint32_t load[PER_LANE], count[PER_LANE];
+#pragma unroll
+        for (int j = 0; j < PER_LANE; ++j) { load[j] = (lane + 32 * j < bins) ? 0u : 0xffffffffu; count[j] = 0; }
+        for (int i = 0; i < n_items; ++i) {
+            const unsigned long long key = keys[i];
+            const uint32_t c = 0xffffffffu - (uint32_t)(key >> 32);
+            if (c == 0) break;   // the rest have no rows
+            uint32_t best = 0xffffffffu; int bj = 0;
+#pragma unroll
+            for (int j = 0; j < PER_LANE; ++j)
+                if (load[j] < best) { best = load[j]; bj = j; }
+            const uint32_t m = __reduce_min_sync(0xffffffffu, best);
+            // among the lanes that hold the minimum, the lowest bin index wins: bins of lane l are l + 32 j
+            const uint32_t cand = (best == m) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
+            const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
+            if (cand == win && best == m) {
+#pragma unroll
+                for (int j = 0; j < PER_LANE; ++j)
+                    if (j == bj) {
+                        keys[i] = ((unsigned long long)((win << 16) | count[j]) << 32) | (uint32_t)key;
+                        load[j] += c; count[j] += 1;
+                    }
+            }
+        }
+        // offsets = exclusive prefix of the counts, in bin order (bin b = lane + 32 j)
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < PER_LANE; ++j)
+            if (lane + 32 * j < bins) offs[lane + 32 * j + 1] = (int)count[j];
+        __syncwarp();
+        if (lane == 0) {
+            offs[0] = 0;
+            for (int b = 0; b < bins; ++b) offs[b + 1] += offs[b];
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int b = tid; b <= bins; b += SCHED_THREADS) off_out[b] = offs[b];
+    const int placed = offs[bins];
+    for (int i = tid; i < placed; i += SCHED_THREADS) {
+        const int item = (int)(uint32_t)keys[i];
+        const uint32_t pl = (uint32_t)(keys[i] >> 32);
+        write_record(a, item_shape(a, item), recs + offs[pl >> 16] + (pl & 0xffffu));
+    }
+}
+
+}  // namespace
+
+int device_sm_count() {
+    static int sm_count[16] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = (dev >= 0 && dev < 16) ? sm_count[dev] : 0;
+    if (sms == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = kNumSMs;
+        if (dev >= 0 && dev < 16) sm_count[dev] = sms;
+    }
+    return sms;
+}
+
+void tc5_plan_items(DecodeArgs& a, bool pair, int sm_count) {
+    a.q_tokens = 128 / a.group;
+    a.tokens_per_item = pair ? 2 * a.q_tokens : a.q_tokens;
+    const int q_len = a.max_q_len > (1 << 20) ? (1 << 20) : a.max_q_len;
+    a.m_blocks = (q_len + a.tokens_per_item - 1) / a.tokens_per_item;
+    const int64_t items = (int64_t)a.num_seqs * a.hkv * a.m_blocks * a.num_splits;
+    a.items_total = (int)(items > (1ll << 30) ? (1ll << 30) : items);
+    int slots = pair ? sm_count / 2 : sm_count;
+    if (slots > kSchedMaxBins) slots = kSchedMaxBins;
+    if (slots < 1) slots = 1;
+    a.bins = (int)(items < slots ? (items < 1 ? 1 : items) : slots);
+}
+
+int launch_decode_sched(const DecodeArgs& a, cudaStream_t st) {
+    if (a.sched_off == nullptr || a.sched_recs == nullptr) return fail(DLX_ERR_WORKSPACE, "decode schedule: no buffer");
+    if (a.bins < 1 || a.bins > kSchedMaxBins) return fail(DLX_ERR_INVALID_ARGUMENT, "decode schedule: %d bins", a.bins);
+    decode_sched_kernel<<<1, SCHED_THREADS, 0, st>>>(a);
+    return check_launch("decode_sched_kernel");
+}
+
+}  // namespace dlx

@@ -27,20 +27,24 @@ import torch
 from . import ops
 from ._lib import DLX_MASK_BLOCK_CAUSAL, DLX_MASK_FULL
 
-_SM_COUNT = 148  # B200
-
 _MASKS = {None: DLX_MASK_FULL, "bd_full": DLX_MASK_FULL, "varlen_full": DLX_MASK_FULL,
           "d2f_block_causal": DLX_MASK_BLOCK_CAUSAL}
 
 
 def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
-                           v_cache: torch.Tensor, scale: float, attn_metadata) -> torch.Tensor:
+                           v_cache: torch.Tensor, scale: float, attn_metadata, out: "torch.Tensor | None" = None
+                           ) -> torch.Tensor:
     """``q [sumQ, Hq, hd]``, ``k/v [sumQ, Hkv, hd]``, unified caches ``[NB, PAGE, Hkv, hd]`` ->
-    new tensor ``o [sumQ, Hq, hd]`` in q's dtype."""
+    new tensor ``o [sumQ, Hq, hd]`` in q's dtype (or ``out``, additive keyword, when given).
+
+    Optional metadata attributes (all additive): ``mask_mode``, ``num_splits``, and ``check_status``:
+    when true the call synchronises afterwards, reads the kernels' status word and raises if a bounded
+    wait inside a kernel gave up (debugging aid; off by default)."""
     md = attn_metadata
     mode = md.decode_mode
     if mode not in ("static", "varlen"):
         raise ValueError(f"unknown decode_mode {mode!r}")
+    ops._need_cuda(q, k, v, k_cache, v_cache)
     mask_name = getattr(md, "mask_mode", None)
     if mask_name not in _MASKS:
         raise ValueError(f"unknown mask_mode {mask_name!r}")
@@ -52,30 +56,51 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     if mode == "varlen":
         max_kv = int(getattr(md, "max_seqlen_k", 0) or 0)  # cumulates ctx+new in this mode
     cu_kv = md.cu_seqlens_k if mode == "static" else None
-    num_splits = int(getattr(md, "num_splits", 0) or os.environ.get("DLX_NUM_SPLITS", 0))
-    return ops.decode_attn(q, k, v, k_cache, v_cache, md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv,
-                           float(scale), max_q, max_kv, _MASKS[mask_name], dbs, num_splits, _longest_first(md, k))
+    num_splits = int(getattr(md, "num_splits", 0) or _ENV_NUM_SPLITS)
+    args = (md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv, float(scale), max_q, max_kv, _MASKS[mask_name],
+            dbs, num_splits)
+    sched = _schedule(md, q, k, k_cache, v_cache, args)
+    if out is None:
+        o = ops.decode_attn(q, k, v, k_cache, v_cache, *args, sched)
+    else:
+        ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, sched)
+        o = out
+    if getattr(md, "check_status", False):
+        bits, site, tile, cta = ops.device_status()
+        if bits & 1:
+            raise RuntimeError(f"decode attention: a bounded wait gave up (site {site}, tile {tile}, CTA {cta}); "
+                               "the output of this call is incomplete")
+    return o
 
 
-def _longest_first(md, k) -> "torch.Tensor | None":
-    """Sequence order for the kernel's grid: longest context first, so that the in-order CTA dispatch
-    behaves like a longest-processing-time schedule when there are more (sequence, KV head) pairs than
-    SMs.  One device-side argsort per metadata state (no host sync), memoised on the metadata object:
-    all layers of a step share it.  The memo is keyed on the context_lens tensor and its version."""
-    ctx = md.context_lens
-    n = int(ctx.numel())
-    if n * int(k.shape[1]) <= _SM_COUNT or os.environ.get("DLX_NO_SEQ_ORDER"):
-        return None
-    key = (ctx.data_ptr(), ctx._version, n)
-    memo = getattr(md, "_dlx_seq_order", None)
+_ENV_NUM_SPLITS = int(os.environ.get("DLX_NUM_SPLITS", "0"))
+_captured_schedules = []   # schedules made inside a stream capture: the graph reads them on every replay
+
+
+def _schedule(md, q, k, k_cache, v_cache, args) -> "torch.Tensor | None":
+    """The step's schedule (``ops.decode_schedule``): built by the first layer call that sees a metadata
+    state and shared by the others through a memo on the metadata object.  The memo is keyed on the
+    metadata tensors (storage and in-place version), the shapes that shape the plan, and the capture id of
+    the current stream: inside a CUDA-graph capture the first layer call always records a planning launch,
+    so a replay after the runner refilled its static buffers (diffulex/strategy/block_diffusion/engine/
+    model_runner.py:183-195) plans from the new lengths."""
+    block_tables, context_lens, cu_q, cu_kv = args[0], args[1], args[2], args[3]
+    cap = ops.stream_capture_id()
+    key = (cap, ops.DECODE_KERNEL, q.shape[0], q.shape[1], k.shape[1], k_cache.shape[1], args[5:],
+           tuple((t.data_ptr(), t._version, t.numel()) if t is not None else None
+                 for t in (block_tables, context_lens, cu_q, cu_kv)))
+    memo = getattr(md, "_dlx_schedule", None)
     if memo is not None and memo[0] == key:
         return memo[1]
-    order = torch.argsort(ctx, descending=True, stable=True).to(torch.int32)
+    sched = ops.decode_schedule(q, k, k_cache, v_cache, *args)
     try:
-        md._dlx_seq_order = (key, order)
+        md._dlx_schedule = (key, sched)
     except AttributeError:
         pass
-    return order
+    if cap and sched is not None:
+        _captured_schedules.append(sched)
+        del _captured_schedules[:-64]
+    return sched
 
 
 def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,

@@ -89,9 +89,14 @@ def _(k_cache, v_cache, block_tables, context_lens, seq_lens, cu_seqlens_q, cu_s
 
 
 # ---- decode attention --------------------------------------------------------------------------
+# Which decode kernel the calls ask for: 0 auto, 1 mma.sync kernel, 2 tcgen05 kernel (one CTA per item),
+# 3 tcgen05 kernel (one CTA pair per item).  Read from DLX_DECODE_KERNEL once, at import; tests set the attribute.
+DECODE_KERNEL = int(os.environ.get("DLX_DECODE_KERNEL", "0"))
+
+
 def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
                    scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits,
-                   seq_order=None) -> DecodeAttnParams:
+                   schedule=None) -> DecodeAttnParams:
     if q.dtype not in _DTYPES:
         raise ValueError(f"decode attention is built for bf16, got {q.dtype}")
     total_q, hq, hd = q.shape
@@ -120,14 +125,45 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
     p.context_lens = context_lens.data_ptr()
     p.cu_seqlens_q = cu_seqlens_q.data_ptr()
     p.cu_seqlens_kv = cu_seqlens_kv.data_ptr() if cu_seqlens_kv is not None else None
-    p.seq_order = seq_order.data_ptr() if seq_order is not None else None
+    if schedule is not None:
+        p.schedule, p.schedule_bytes = schedule.data_ptr(), schedule.numel() * schedule.element_size()
     p.total_q, p.num_seqs = total_q, cu_seqlens_q.numel() - 1
     p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
     p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
     p.mask_mode, p.diffusion_block_size = mask_mode, diffusion_block_size
-    p.num_splits, p.kernel = num_splits, int(os.environ.get("DLX_DECODE_KERNEL", "0"))  # 0 auto, 1 mma.sync, 2 tcgen05
+    p.num_splits, p.kernel = num_splits, DECODE_KERNEL
     p.scale = scale
     return p
+
+
+def _check_decode_metadata(q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, schedule=None):
+    for name, t in (("block_tables", block_tables), ("context_lens", context_lens), ("cu_seqlens_q", cu_seqlens_q),
+                    ("cu_seqlens_kv", cu_seqlens_kv)):
+        if t is not None and t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block_tables must be [num_seqs, max_blocks] with contiguous rows")
+    if schedule is not None and (schedule.dtype != torch.uint8 or not schedule.is_contiguous()):
+        raise ValueError("schedule must be the uint8 buffer returned by decode_schedule")
+
+
+def _decode_launch(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                   max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, schedule) -> None:
+    _need_cuda(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, schedule)
+    _check_decode_metadata(q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, schedule)
+    p = _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
+                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, schedule)
+    handle = _lib.lib()
+    ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
+    if ws_bytes < 0:
+        check(int(-ws_bytes))
+    if schedule is not None:  # the prepared schedule replaces the one the call would plan into its workspace
+        ws_bytes -= handle.dlx_decode_attn_schedule_bytes(ctypes.byref(p))
+    ws = None
+    if ws_bytes > 0:
+        ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws_bytes
+    check(handle.dlx_decode_attn(ctypes.byref(p), _stream()))
 
 
 @torch.library.custom_op("dlx_b200::decode_attn", mutates_args=())
@@ -135,35 +171,67 @@ def decode_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torc
                 block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
                 cu_seqlens_kv: Optional[torch.Tensor], scale: float, max_q_len: int, max_kv_len: int,
                 mask_mode: int, diffusion_block_size: int, num_splits: int,
-                seq_order: Optional[torch.Tensor] = None) -> torch.Tensor:
-    _need_cuda(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, seq_order)
-    if seq_order is not None and (seq_order.numel() != cu_seqlens_q.numel() - 1 or not seq_order.is_contiguous()):
-        raise ValueError("seq_order must be a contiguous int32 permutation of the sequences")
-    for name, t in (("block_tables", block_tables), ("context_lens", context_lens), ("cu_seqlens_q", cu_seqlens_q),
-                    ("cu_seqlens_kv", cu_seqlens_kv), ("seq_order", seq_order)):
-        if t is not None and t.dtype != torch.int32:
-            raise ValueError(f"{name} must be int32")
-    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
-        raise ValueError("block_tables must be [num_seqs, max_blocks] with contiguous rows")
+                schedule: Optional[torch.Tensor] = None) -> torch.Tensor:
     out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), device=q.device, dtype=q.dtype)
-    p = _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
-                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, seq_order)
-    handle = _lib.lib()
-    ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
-    if ws_bytes < 0:
-        check(int(-ws_bytes))
-    ws = None
-    if ws_bytes > 0:
-        ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
-        p.workspace, p.workspace_bytes = ws.data_ptr(), ws_bytes
-    check(handle.dlx_decode_attn(ctypes.byref(p), _stream()))
+    _decode_launch(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                   max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, schedule)
     return out
 
 
 @decode_attn.register_fake
 def _(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale, max_q_len,
-      max_kv_len, mask_mode, diffusion_block_size, num_splits, seq_order=None):
+      max_kv_len, mask_mode, diffusion_block_size, num_splits, schedule=None):
     return q.new_empty(q.shape)
+
+
+@torch.library.custom_op("dlx_b200::decode_attn_out", mutates_args=("out",))
+def decode_attn_out(out: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                    v_cache: torch.Tensor, block_tables: torch.Tensor, context_lens: torch.Tensor,
+                    cu_seqlens_q: torch.Tensor, cu_seqlens_kv: Optional[torch.Tensor], scale: float, max_q_len: int,
+                    max_kv_len: int, mask_mode: int, diffusion_block_size: int, num_splits: int,
+                    schedule: Optional[torch.Tensor] = None) -> None:
+    """``decode_attn`` into a caller-owned ``out`` ([total_q, Hq, hd], contiguous heads, any row stride)."""
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must have q's shape and dtype")
+    _decode_launch(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                   max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, schedule)
+
+
+def decode_schedule(q: torch.Tensor, k: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                    cu_seqlens_kv: Optional[torch.Tensor], scale: float, max_q_len: int, max_kv_len: int,
+                    mask_mode: int, diffusion_block_size: int, num_splits: int) -> Optional[torch.Tensor]:
+    """The per-step half of decode attention (C ABI: dlx_decode_attn_prepare): one small launch that turns
+    the step's metadata into the packed, placed work-item records every layer call of the step then reads.
+    Returns the schedule buffer to pass as ``schedule``, or None when the kernel that serves these shapes
+    takes none.  No host sync; capturable."""
+    _need_cuda(q, k, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv)
+    _check_decode_metadata(q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv)
+    p = _decode_params(q, k, k, k_cache, v_cache, q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
+                       scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
+    handle = _lib.lib()
+    n = handle.dlx_decode_attn_schedule_bytes(ctypes.byref(p))
+    if n < 0:
+        check(int(-n))
+    if n == 0 or p.num_seqs == 0 or p.total_q == 0:
+        return None
+    sched = torch.empty(n, device=q.device, dtype=torch.uint8)
+    check(handle.dlx_decode_attn_prepare(ctypes.byref(p), sched.data_ptr(), n, _stream()))
+    return sched
+
+
+def stream_capture_id() -> int:
+    """Capture sequence id of the current stream (0 when it is not being captured)."""
+    cid = ctypes.c_uint64(0)
+    check(_lib.lib().dlx_stream_capture_id(_stream(), ctypes.byref(cid)))
+    return int(cid.value)
+
+
+def device_status() -> tuple:
+    """(bits, site, tile, cta) of the tcgen05 kernels' status word; synchronises and clears it."""
+    out = (ctypes.c_int32 * 4)()
+    check(_lib.lib().dlx_debug_device_status(out))
+    return tuple(int(x) for x in out)
 
 
 def planned_num_splits(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
@@ -177,5 +245,5 @@ def planned_num_splits(q, k, v, k_cache, v_cache, block_tables, context_lens, cu
     return n
 
 
-__all__ = ["store_kvcache_unified", "store_kvcache_distinct", "load_kvcache", "decode_attn", "planned_num_splits",
-           "DlxError"]
+__all__ = ["store_kvcache_unified", "store_kvcache_distinct", "load_kvcache", "decode_attn", "decode_attn_out",
+           "decode_schedule", "stream_capture_id", "device_status", "planned_num_splits", "DlxError"]

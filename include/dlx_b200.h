@@ -117,11 +117,13 @@ typedef struct dlx_decode_attn_params {
     const int32_t* context_lens; /* [num_seqs]                                                         */
     const int32_t* cu_seqlens_q; /* [num_seqs + 1]                                                     */
     const int32_t* cu_seqlens_kv;/* [num_seqs + 1] in-flight offsets, or NULL (= cu_seqlens_q)         */
-    const int32_t* seq_order;    /* optional [num_seqs] permutation: sequence taken by the i-th group of
-                                    CTAs.  Longest context first lets the hardware's in-order CTA dispatch
-                                    act as a longest-processing-time schedule.  NULL = identity          */
-    void* workspace;             /* split-K scratch, >= dlx_decode_attn_workspace_bytes(); may be NULL
-                                    when that returns 0                                                */
+    const void* schedule;        /* optional: a schedule written by dlx_decode_attn_prepare for THESE
+                                    parameters and the current contents of context_lens / cu_seqlens_* /
+                                    block_tables.  NULL: the call plans itself (one more small launch) into
+                                    the tail of `workspace`                                            */
+    int64_t schedule_bytes;
+    void* workspace;             /* scratch, >= dlx_decode_attn_workspace_bytes(): split-K partials and, when
+                                    `schedule` is NULL, the schedule.  May be NULL when nothing is needed */
     int64_t workspace_bytes;
     int64_t q_row_stride, k_row_stride, v_row_stride, out_row_stride;
     int64_t cache_page_stride, cache_token_stride;
@@ -136,33 +138,57 @@ typedef struct dlx_decode_attn_params {
     int32_t mask_mode;           /* DLX_MASK_*                                                         */
     int32_t diffusion_block_size;
     int32_t num_splits;          /* 0 = choose; >= 1 forces that many key-range splits per sequence    */
-    int32_t kernel;              /* 0 = choose; 1 = mma.sync kernel; 2 = tcgen05 kernel (if eligible)   */
+    int32_t kernel;              /* 0 = choose; 1 = mma.sync kernel; 2 = tcgen05 kernel, one CTA per item;
+                                    3 = tcgen05 kernel, one CTA pair per item (if eligible)            */
     float scale;                 /* softmax scale, hd^-1/2 in every shipped model                      */
 } dlx_decode_attn_params;
 
-/* Bytes of scratch dlx_decode_attn needs for these parameters (0 when no split is used), or a
- * negative dlx_status.  Depends only on host-known sizes, never on device contents. */
+/* Bytes of scratch dlx_decode_attn needs for these parameters when it plans itself (split-K partials
+ * + schedule; 0 when neither is used), or a negative dlx_status.  Depends only on host-known sizes,
+ * never on device contents. */
 int64_t dlx_decode_attn_workspace_bytes(const dlx_decode_attn_params* p);
 /* Number of splits dlx_decode_attn will use for these parameters. */
 int32_t dlx_decode_attn_num_splits(const dlx_decode_attn_params* p);
 int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream);
 
 /*
+ * The per-step half of decode attention: what the reference's model runner computes on the host before
+ * every decode step (diffulex/strategy/block_diffusion/engine/model_runner.py:125-158 and
+ * diffulex/strategy/d2f/engine/model_runner.py:150-243: per-sequence lengths and offsets for the kernels),
+ * done on the device.  dlx_decode_attn_prepare launches one small kernel that reads context_lens,
+ * cu_seqlens_q / cu_seqlens_kv and block_tables and writes a schedule: one packed record per (sequence,
+ * KV head, query-token block, key-range split) with its lengths, offsets and first page ids, placed on the
+ * persistent CTAs longest first.  Every layer of the step then passes that buffer as `schedule`.  The launch
+ * can be captured: a replayed graph re-plans from the refilled metadata buffers.  Only the pointers and sizes
+ * named above are read; q / k / v / caches / out may be NULL here.
+ * dlx_decode_attn_schedule_bytes: bytes of the buffer (0: the kernel chosen for these parameters takes no
+ * schedule, prepare is a no-op), or a negative dlx_status.
+ */
+int64_t dlx_decode_attn_schedule_bytes(const dlx_decode_attn_params* p);
+int dlx_decode_attn_prepare(const dlx_decode_attn_params* p, void* schedule, int64_t schedule_bytes, void* stream);
+/* Library plumbing: *id = the capture sequence id of `stream` while it is being captured, else 0 (lets a
+ * caller keep one prepared schedule per captured graph). */
+int dlx_stream_capture_id(void* stream, uint64_t* id);
+
+/*
  * Decode attention for callers that cannot hand over scratch memory.  No counterpart in the reference.
  *
- * Same operator, same parameters and same results as dlx_decode_attn, but the split-K scratch (partial
- * outputs and log-sum-exps of the key-range splits) is a fixed array inside the library's device image
+ * Same operator, same parameters and same results as dlx_decode_attn, but the scratch (partial
+ * outputs and log-sum-exps of the key-range splits, the launch's schedule) is a fixed array inside the library's device image
  * instead of `p->workspace` (which is ignored here).  Meant for hosts that own no allocator on the device
  * side of the call: a serving loop whose memory pool is sized and frozen at start-up, a plugin that is
  * handed tensors but may not call cudaMalloc (or torch's allocator) from its callback, code running
  * under a memory budget where a late allocation failure is not an option.  The function calls no
  * allocating routine of CUDA or of any library; q, k, v, caches, tables and `out` still come from the caller.
  *
- *  - Capacity: dlx_static_scratch_bytes() (32 MiB).  Every GPU that loads this library carries the array
- *    from load to exit.  A call that would need more (see dlx_decode_attn_workspace_bytes) returns
- *    DLX_ERR_WORKSPACE with a message and launches nothing; lower num_splits or use dlx_decode_attn.
+ *  - Capacity: dlx_static_scratch_bytes() (32 MiB).  A call that would need more (see
+ *    dlx_decode_attn_workspace_bytes) returns DLX_ERR_WORKSPACE with a message and launches nothing; lower
+ *    num_splits or use dlx_decode_attn.
  *  - The first call on a device looks the array's device address up (with that device current) and keeps
- *    it; make that first call outside of any stream capture.
+ *    it.  That look-up is also what makes the CUDA runtime load this part of the library, the 32 MiB array
+ *    included, on that device, so it is the one call here that can still fail for lack of device memory:
+ *    make it at start-up, outside of any stream capture.  From then on the GPU holds the array until the
+ *    process exits.  The kept address does not survive a cudaDeviceReset; devices 0..63 are tracked.
  *  - All calls on a device share the one array, which keeps whatever the last call left in it.  Nothing in
  *    it has to start at zero: every entry a call reads was written by that call.  Two calls whose kernels
  *    may overlap on the GPU (different streams, no dependency) race on it; order them.
@@ -171,23 +197,12 @@ int64_t dlx_static_scratch_bytes(void);
 int dlx_decode_attn_static_scratch(const dlx_decode_attn_params* p, void* stream);
 
 /*
- * Debug aid with no counterpart in the reference.  out[0] is a bit set: bit 0 = a bounded wait inside the
- * tcgen05 kernel expired (every wait there is bounded; the CTA then stops early instead of trapping, and
- * out[1..3] hold the wait site, the tile and the CTA that gave up first); bit 1 = scores more than 100
- * log2-units above the softmax reference of their row (the row maximum of the first key tile) were
- * clamped there: the kernel never rescales its accumulator, so that is its exponent headroom.  This call
- * synchronises the device, copies the word to the HOST array `out` and clears it.  out[0] == 0: neither
- * happened since the last call.
+ * Debug aid with no counterpart in the reference.  out[0] bit 0 = a bounded wait inside a tcgen05 kernel
+ * expired (every wait there is bounded; the CTA then stops early instead of trapping, and out[1..3] hold
+ * the wait site, the tile and the CTA that gave up first).  This call synchronises the device, copies the
+ * word to the HOST array `out` and clears it.  out[0] == 0: it did not happen since the last call.
  */
 int dlx_debug_device_status(int32_t out[4]);
-
-/*
- * Debug aid with no counterpart in the reference: the switch of the kernel's event recording.  Only a
- * library built with -DDLX_TC5_PROFILE=1 records anything (CTA 0's event times, every CTA's entry and exit
- * time); in the regular build the switch is inert.  The call synchronises, copies 24 legacy counters
- * (all zero) to the HOST array `out` (may be NULL), clears them, and sets the switch to `enable`.
- */
-int dlx_debug_profile(int enable, uint64_t out[24]);
 
 #ifdef __cplusplus
 }

@@ -28,7 +28,10 @@ def good_params(**over):
     from diffulex_b200._lib import DecodeAttnParams
     p = DecodeAttnParams()
     p.struct_bytes = ctypes.sizeof(DecodeAttnParams)
-    p.total_q, p.num_seqs, p.max_blocks = 2048, 64, 9
+    p.total_q, p.num_seqs, p.max_blocks, p.num_pages = 2048, 64, 9, 600
+    p.q_row_stride = p.out_row_stride = 28 * 128
+    p.k_row_stride = p.v_row_stride = p.cache_token_stride = 4 * 128
+    p.cache_page_stride = 256 * 4 * 128
     p.num_q_heads, p.num_kv_heads, p.head_dim, p.page_size = 28, 4, 128, 256
     p.max_q_len, p.max_kv_len, p.mask_mode, p.diffusion_block_size = 32, 0, 0, 32
     p.scale = 128 ** -0.5
@@ -86,13 +89,22 @@ def test_store_and_load_validation_statuses(lib):
 def test_split_planning_is_host_only_and_sized_right(lib):
     n = lambda p: lib.dlx_decode_attn_num_splits(ctypes.byref(p))
     ws = lambda p: lib.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
-    # 64 seqs x 4 KV heads = 256 CTAs >= 148 slots, contexts <= 2336 keys: one pass, no scratch
+    sb = lambda p: lib.dlx_decode_attn_schedule_bytes(ctypes.byref(p))
+    # 64 seqs x 4 KV heads = 256 items of 224 rows on 74 CTA pairs, contexts <= 2336 keys: one pass; the only
+    # scratch is the schedule (1 KiB of offsets + one 128-byte record per item) when the call plans itself
     p = good_params()
-    assert n(p) == 1 and ws(p) == 0
-    # forced splits: lse [splits, rows] (256-byte padded) + partial O [splits, rows, hd] fp32
+    assert n(p) == 1 and sb(p) == 1024 + 256 * 128 and ws(p) == sb(p)
+    # the single-CTA tcgen05 kernel cuts the 224 rows into two items
+    assert sb(good_params(kernel=2)) == 1024 + 512 * 128
+    # the mma.sync kernel takes no schedule
+    assert sb(good_params(kernel=1)) == 0 and ws(good_params(kernel=1)) == 0
+    # forced splits: lse [splits, rows] (256-byte padded) + partial O [splits, rows, hd] fp32 + schedule
     p = good_params(num_splits=3)
     rows = 2048 * 28
-    assert n(p) == 3 and ws(p) == ((3 * rows * 4 + 255) // 256) * 256 + 3 * rows * 128 * 4
+    assert sb(p) == 1024 + 3 * 256 * 128
+    assert n(p) == 3 and ws(p) == ((3 * rows * 4 + 255) // 256) * 256 + 3 * rows * 128 * 4 + sb(p)
+    # preparing a schedule needs the metadata pointers and a buffer of that size
+    assert lib.dlx_decode_attn_prepare(ctypes.byref(p), None, 0, None) == 1
     # few sequences: split to fill 148 SMs
     p = good_params(num_seqs=2, total_q=64)
     assert n(p) > 1

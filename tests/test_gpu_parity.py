@@ -16,6 +16,7 @@ from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, 
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 2e-2, 1e-2
+KERNELS = {"auto": 0, "mma": 1, "tc5": 2, "pair": 3}
 
 
 @pytest.fixture(scope="module")
@@ -111,14 +112,18 @@ def test_load_bit_exact(name, dlx, golden_dir):
 @pytest.mark.parametrize("name", list(ATTN_CASES) + list(D2F_CASES))
 @pytest.mark.parametrize("mode", ["static", "varlen"])
 @pytest.mark.parametrize("num_splits", [0, 1, 3])
-@pytest.mark.parametrize("kernel", ["auto", "mma"])
+@pytest.mark.parametrize("kernel", ["auto", "tc5", "pair", "mma"])
 def test_attention_matches_golden_and_oracle(name, mode, num_splits, kernel, dlx, golden_dir, monkeypatch):
-    # "auto" takes the tcgen05 kernel where the shape is eligible (head_dim 128)
-    # and the mma.sync kernel elsewhere; "mma" forces the mma.sync kernel everywhere
-    monkeypatch.setenv("DLX_DECODE_KERNEL", {"auto": "0", "mma": "1"}[kernel])
+    # "auto": head_dim 128 goes to a tcgen05 kernel (the CTA-pair kernel for more than 128 packed rows per KV head,
+    # the single-CTA kernel otherwise), everything else to the mma.sync kernel; the other three force one kernel.
+    # Forcing "pair" on a short query block runs the pair with an idle second CTA.
+    from diffulex_b200 import ops
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
     meta = json.loads((golden_dir / "attn_golden.json").read_text())[name]
     want_sel = torch.from_numpy(np.load(golden_dir / "attn_golden.npz")[name])
     p = attn_problem(ATTN_CASES.get(name) or D2F_CASES[name])
+    if kernel in ("tc5", "pair") and p.geometry.head_dim != 128:
+        pytest.skip("the tcgen05 kernels serve head_dim 128")
     want = oracle_out(p)
     pd = to_dev(p)
     o = run_decode(dlx, pd, mode, num_splits)
@@ -282,13 +287,18 @@ def test_cfg5_attention_properties(dlx, cfg5_problem):
         torch.testing.assert_close(o_auto[q0:q1].float().cpu(), want, atol=ATOL, rtol=RTOL)
 
 
-def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
-    """Forcing the tcgen05 kernel works on eligible shapes (head_dim 128: 7 and 4 query heads per KV head
-    here), is refused on an ineligible one (head_dim 64), and the kernel's bounded waits never ran
+def device_status():
+    from diffulex_b200 import ops
+    return list(ops.device_status())
+
+
+@pytest.mark.parametrize("kernel", ["tc5", "pair"])
+def test_tcgen05_kernels_are_taken_and_no_wait_expired(kernel, dlx, monkeypatch):
+    """Forcing a tcgen05 kernel works on eligible shapes (head_dim 128: 7 and 4 query heads per KV head
+    here), is refused on an ineligible one (head_dim 64), and the kernels' bounded waits never ran
     out during this test session."""
-    import ctypes
-    from diffulex_b200 import _lib
-    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
+    from diffulex_b200 import _lib, ops
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
     p = attn_problem(ATTN_CASES["cfg1"])
     for splits in (0, 2):
         o = run_decode(dlx, to_dev(p), "static", splits)
@@ -297,17 +307,18 @@ def test_tcgen05_kernel_is_taken_and_no_wait_expired(dlx, monkeypatch):
     torch.testing.assert_close(run_decode(dlx, to_dev(p4)).float().cpu(), oracle_out(p4), atol=ATOL, rtol=RTOL)
     with pytest.raises(_lib.DlxError):
         run_decode(dlx, to_dev(attn_problem(ATTN_CASES["ref_head_dim_64"])))
-    st = (ctypes.c_int32 * 4)()
-    assert _lib.lib().dlx_debug_device_status(st) == 0
-    assert list(st) == [0, 0, 0, 0], f"a bounded wait expired: {list(st)}"
+    st = device_status()
+    assert st == [0, 0, 0, 0], f"a bounded wait expired: {st}"
 
 
-def test_more_rounds_than_the_item_table_holds(dlx, monkeypatch):
-    """300 sequences x 32 KV heads = 9600 work items, i.e. 65 rounds on 148 persistent CTAs: one more than the
-    kernel's shared-memory item table holds, so the instantiation that decodes items per role is the one that
-    runs (the large configurations reach it only with forced key-range splits)."""
+@pytest.mark.parametrize("kernel", ["tc5", "pair"])
+def test_more_items_than_the_placement_sorts_and_the_item_table_holds(kernel, dlx, monkeypatch):
+    """300 sequences x 32 KV heads = 9600 work items: more than the schedule kernel sorts (it deals them
+    round-robin instead) and 65 / 130 rounds per persistent CTA / CTA pair: more than the kernels' shared-memory
+    record tables hold, so later rounds are read from the global records."""
+    from diffulex_b200 import ops
     from diffulex_b200.workload import MASK_BD_FULL, make_problem, small_workload
-    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
     rng = np.random.default_rng(5)
     ctx = rng.integers(0, 200, size=300).tolist()
     w = small_workload("many_items", 32, 32, 128, 32, 4, ctx, [4] * 300, MASK_BD_FULL, 41)
@@ -316,30 +327,135 @@ def test_more_rounds_than_the_item_table_holds(dlx, monkeypatch):
     torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)
 
 
-def test_out_of_range_scores_are_clamped_flagged_and_finite(dlx, monkeypatch):
-    """A key whose score lies more than 100 log2-units above the softmax reference of its row (here ~130 nats
-    above everything else) uses up the exponent headroom of the fixed-reference softmax: the kernel clamps
-    it, sets bit 1 of the device status word, and the output stays finite; with ONE such key the clamped
-    result still equals the exact one (that key's V row)."""
-    import ctypes
-    from diffulex_b200 import _lib
+@pytest.mark.parametrize("kernel", ["tc5", "pair"])
+def test_scores_far_above_the_first_tile_are_exact(kernel, dlx, monkeypatch):
+    """The tcgen05 kernels scale a row's exponentials by the maximum of the item's FIRST key tile and never
+    rescale.  Two keys whose scores lie ~200 and ~180 log2-units above everything else (in a later tile) leave the
+    range in which that is exact; the kernels notice (row sum of the tile) and compute the item again with a
+    running maximum, so the output still matches the oracle: their weights differ by 2^-20, i.e. the output
+    is the higher key's V row."""
+    from diffulex_b200 import ops
     from diffulex_b200.workload import MASK_BD_FULL, make_problem, small_workload
-    monkeypatch.setenv("DLX_DECODE_KERNEL", "2")
-    w = small_workload("clamp", 28, 4, 128, 64, 32, [300, 520], [32, 32], MASK_BD_FULL, 77)
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
+    w = small_workload("hot_keys", 28, 4, 128, 64, 32, [300, 520], [32, 32], MASK_BD_FULL, 77)
     p = make_problem(w, device="cpu", values="numpy")
     u = p.q[0, 0].clone()
     p.q[:] = u                                         # every row asks the same question ...
-    for s in range(2):                                 # ... and key 5 of every sequence answers it 12 times over
+    for s in range(2):                                 # ... and keys 5 and 9 of every sequence answer it loudly
         page = int(p.block_tables[s, 0])
         p.k_cache[page, 5] = (12.0 * u).to(p.k_cache.dtype)
-    st = (ctypes.c_int32 * 4)()
-    assert _lib.lib().dlx_debug_device_status(st) == 0   # clear
+        p.k_cache[page, 9] = (11.0 * u).to(p.k_cache.dtype)
+    want = oracle_out(p)
+    for splits in (1, 2):
+        o = run_decode(dlx, to_dev(p), "static", splits)
+        assert torch.isfinite(o).all()
+        torch.testing.assert_close(o.float().cpu(), want, atol=ATOL, rtol=RTOL)
+    # mixed case: only sequence 1 is out of range, sequence 0 takes the fast path
+    page = int(p.block_tables[0, 0])
+    p.k_cache[page, 5] = p.k_cache[page, 6]
+    p.k_cache[page, 9] = p.k_cache[page, 6]
+    o = run_decode(dlx, to_dev(p), "static", 1)
+    torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)
+    assert device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("kernel", ["tc5", "pair"])
+def test_rows_that_see_nothing_of_the_first_tile_are_exact(kernel, dlx, monkeypatch):
+    """Block-causal rows of an early in-flight block see none of the keys of the item's first tile (a late one),
+    so their softmax reference comes from keys hidden to them.  Here those hidden keys score ~200 log2-units
+    above the visible ones: every exponential of such a row underflows, the kernels notice (row sum ~ 0 although
+    keys are visible) and recompute the item exactly."""
+    from diffulex_b200 import ops
+    from diffulex_b200.workload import MASK_D2F_BLOCK_CAUSAL, make_problem, small_workload
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
+    w = small_workload("hidden_first_tile", 28, 4, 128, 64, 32, [64, 10], [256, 224], MASK_D2F_BLOCK_CAUSAL, 78)
+    p = make_problem(w, device="cpu", values="numpy")
+    u = p.q[0, 0].clone()
+    p.q[:] = u
+    p.k[128:] = (12.0 * u).to(p.k.dtype)               # in-flight keys 128.. of sequence 0 (and all of sequence 1)
     want = oracle_out(p)
     o = run_decode(dlx, to_dev(p), "static", 1)
     assert torch.isfinite(o).all()
     torch.testing.assert_close(o.float().cpu(), want, atol=ATOL, rtol=RTOL)
-    assert _lib.lib().dlx_debug_device_status(st) == 0   # reads and clears
-    assert st[0] == 2 and list(st)[1:] == [0, 0, 0], f"expected only the clamp flag: {list(st)}"
+    assert device_status() == [0, 0, 0, 0]
+
+
+def parse_schedule(sched, bins):
+    """(offsets, records) of a schedule buffer: int32 offsets[bins + 1] in a 1 KiB header, then 32-int records
+    (seq, kvh, mb, split, q0, qn, ctx, kv0, nnew, t0, n, flags, first_page, n_pages, limit, -, pages[16])."""
+    raw = sched.cpu().numpy().view(np.int32)
+    off = raw[: bins + 1]
+    recs = raw[256:].reshape(-1, 32)
+    return off, recs
+
+
+def test_schedule_covers_every_item_once_and_balances(dlx):
+    """The device-built schedule of benchmark configuration 2: 256 (sequence, KV head) items on 74 CTA pairs, every
+    item exactly once, longest first inside a pair, loads within one item of each other, page ids attached."""
+    from diffulex_b200 import ops
+    from diffulex_b200.workload import make_problem, named_workload
+    p = make_problem(named_workload("cfg2"), device="cuda", values="torch")
+    md = p.metadata("static")
+    sched = ops.decode_schedule(p.q, p.k, p.k_cache, p.v_cache, p.block_tables, p.context_lens, p.cu_seqlens_q,
+                                p.cu_seqlens_k, p.scale, md.max_seqlen_q, 0, p.mask_mode, 32, 0)
+    off, recs = parse_schedule(sched, 74)
+    assert off[0] == 0 and off[74] == 256 and np.all(np.diff(off) >= 1)
+    recs = recs[:256]
+    assert sorted(map(tuple, recs[:, :4])) == sorted((s, h, 0, 0) for s in range(64) for h in range(4))
+    ctx = p.host_context_lens
+    bt = p.block_tables.cpu().numpy()
+    loads = []
+    for b in range(74):
+        mine = recs[off[b]:off[b + 1]]
+        assert np.all(np.diff(mine[:, 10]) <= 0), "longest item first"
+        loads.append(int(mine[:, 10].sum() + len(mine)))
+        for r in mine:
+            s = int(r[0])
+            assert r[6] == ctx[s] and r[5] == 32 and r[8] == 32 and r[9] == 0 and r[11] == 1
+            assert r[10] == (ctx[s] + 32 + 127) // 128 and r[14] == ctx[s] + 32
+            last_page = (ctx[s] - 1) // 256
+            assert r[12] == max(0, last_page - 15) and r[13] == last_page - r[12] + 1
+            assert np.array_equal(r[16:16 + r[13]], bt[s, r[12]:r[12] + r[13]])
+    assert max(loads) - min(loads) <= int(recs[:, 10].max()) + 1
+
+
+def test_captured_step_replans_when_the_metadata_buffers_are_refilled(dlx):
+    """A captured decode step holds its planning launch: after the runner refills the static metadata buffers
+    in place with other lengths (diffulex/strategy/block_diffusion/engine/model_runner.py:183-195), a replay
+    matches the oracle of the NEW step and its schedule follows the new lengths."""
+    from diffulex_b200.workload import MASK_BD_FULL, make_problem, small_workload
+    mk = lambda ctx, seed: make_problem(small_workload("replan", 28, 4, 128, 256, 32, ctx, [32] * 4, MASK_BD_FULL, seed,
+                                                       spare_pages=24), device="cpu", values="numpy")
+    pa, pb = mk([900, 100, 400, 30], 91), mk([60, 950, 200, 300], 92)
+    assert pa.k_cache.shape == pb.k_cache.shape and pa.block_tables.shape == pb.block_tables.shape
+    pd = to_dev(pa)
+    md = pd.metadata("static")
+    md.num_splits = 1
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        dlx.dllm_flash_attn_decode(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, pd.scale, md)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        o1 = dlx.dllm_flash_attn_decode(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, pd.scale, md)
+        o2 = dlx.dllm_flash_attn_decode(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, pd.scale, md)   # second layer: same plan
+    g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(o1.float().cpu(), oracle_out(pa), atol=ATOL, rtol=RTOL)
+    for name in ("q", "k", "v", "k_cache", "v_cache", "block_tables", "context_lens"):
+        getattr(pd, name).copy_(getattr(pb, name))
+    g.replay()
+    torch.cuda.synchronize()
+    want = oracle_out(pb)
+    torch.testing.assert_close(o1.float().cpu(), want, atol=ATOL, rtol=RTOL)
+    assert torch.equal(o1, o2)
+    bins = 16   # 4 sequences x 4 KV heads: one item per CTA pair
+    off, recs = parse_schedule(md._dlx_schedule[1], bins)
+    recs = recs[: off[bins]]
+    new_ctx = pb.host_context_lens
+    assert all(r[6] == new_ctx[r[0]] for r in recs)
+    assert [int(r[0]) for r in recs[:4]] == [1, 1, 1, 1], "the longest sequence of the NEW step comes first"
 
 
 # ---- error behaviour ---------------------------------------------------------------------------

@@ -6,8 +6,9 @@ tensors but is not allowed to allocate, a caller that must not fail on a late ou
 the split-K scratch in a fixed 32 MiB array inside the library.  This test calls it twice in a row
 with key-range splits forced on (so the scratch is really used, and the second call runs over what the
 first one left behind) and compares with `dlx_decode_attn` fed caller-owned scratch.  Both run the same
-kernels, so the outputs are expected to be identical; the comparison still uses the attention
-tolerance of the other GPU tests.  Collected last on purpose (file name), so that a run that stops at
+kernels in the same split order, so the outputs must be bit-identical (a scratch-reuse bug that stays inside
+the attention tolerance would still show); the oracle is checked within the tolerance of the other GPU
+tests.  Collected last on purpose (file name), so that a run that stops at
 the first failure has already executed every other test.
 """
 import ctypes
@@ -60,7 +61,7 @@ def test_static_scratch_entry_point_matches_regular_entry_point():
         outs.append(out)
     torch.cuda.synchronize()
     for out in outs:
-        torch.testing.assert_close(out.float(), out_ref.float(), atol=ATOL, rtol=RTOL)
+        assert torch.equal(out, out_ref)
     want = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
                                         p.cu_seqlens_q, p.cu_seqlens_k, p.scale, p.mask_mode,
                                         p.geometry.diffusion_block_size)
