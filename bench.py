@@ -44,9 +44,9 @@ import numpy as np
 import torch
 
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per decode launch from the committed ncu captures
-# (profiles/), keyed by workload; None until a capture exists for that workload.
-NCU_TRAFFIC_BYTES = {"cfg2": 178511104 + 9658112}  # profiles/decode_attn_tc5_cfg2.md
+# dram__bytes_read.sum + dram__bytes_write.sum per decode launch of the workload, from an ncu capture of this
+# command on two resident layer caches; None where no capture has been taken.
+NCU_TRAFFIC_BYTES = {"cfg2": 178511104 + 9658112}
 
 
 def parse():
@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = the model's)")
     ap.add_argument("--num-splits", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-group", type=int, default=7, help="layers per host<->device copy group of the e2e step")
+    ap.add_argument("--no-strong", action="store_true", help="skip the cfg5 strong-scaling side measurement")
+    ap.add_argument("--no-splitk", action="store_true", help="skip the split-K side measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-store-load", action="store_true", help="skip the store / load bandwidth side measurement")
     ap.add_argument("--only-store-load", action="store_true",
@@ -217,6 +220,116 @@ def store_load_bandwidth(dlx, dev, peak, num_seqs=256):
     return out
 
 
+def pin_cpus(local_rank: int, world: int) -> None:
+    """Give every rank of a multi-GPU run its own slice of the host cores this process may use (the launcher
+    starts all ranks with the same affinity mask, so eight ranks would otherwise share the same cores for
+    their copy and launch loops).  Pinned host buffers are then first touched from those cores."""
+    if world <= 1:
+        return
+    try:
+        cores = sorted(os.sched_getaffinity(0))
+        per = max(1, len(cores) // world)
+        mine = cores[local_rank * per:(local_rank + 1) * per] or cores
+        os.sched_setaffinity(0, mine)
+        torch.set_num_threads(max(1, min(per, 8)))
+    except (AttributeError, OSError):
+        pass
+
+
+def strong_cfg5(dlx, dp, dev, rank, world, peak):
+    """Strong scaling of the scaling-sweep configuration: its 256 sequences (seed fixed) are sharded over the ranks
+    by longest-processing-time on KV tokens, every rank stores and decodes its shard (one layer), and the outputs
+    are gathered over the process group.  Reported: per-rank time, imbalance, aggregate KV GB/s of the slowest rank,
+    the gather's time, and a bit checksum of the gathered tensor against the sum of the ranks' own checksums."""
+    from diffulex_b200.workload import make_problem, named_workload, partition_lpt, shard_workload
+    w_global = named_workload("cfg5")
+    w, owned = shard_workload(w_global, rank, world)
+    parts = (partition_lpt((w_global.context_lens + w_global.new_lens).tolist(), world) if world > 1
+             else [list(range(len(w_global.context_lens)))])
+    p = make_problem(w, device=dev, values="torch")
+    md = p.metadata("static")
+    out = torch.empty_like(p.q)
+
+    def step():
+        dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
+        dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md, out=out)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 5
+    ea.record()
+    for _ in range(n):
+        step()
+    eb.record()
+    torch.cuda.synchronize()
+    ms_local = ea.elapsed_time(eb) / n
+    per_rank = dp.gather_timings(ms_local, dev)
+    bytes_local = float(p.kv_bytes())
+    per_rank_bytes = dp.gather_timings(bytes_local, dev)
+    total_bytes = sum(per_rank_bytes)
+    slowest = max(per_rank)
+    # gather of the outputs (59 MB in total) over the process group, timed on the device
+    q_lens = w_global.new_lens.tolist()
+    full = dp.gather_outputs(out, parts, q_lens)
+    torch.cuda.synchronize()
+    ea.record()
+    full = dp.gather_outputs(out, parts, q_lens)
+    eb.record()
+    torch.cuda.synchronize()
+    gather_ms = dp.max_over_ranks(ea.elapsed_time(eb), dev)
+    bits_sum = lambda t: float(t.contiguous().view(torch.int16).to(torch.int64).sum().item())
+    local_sum = bits_sum(out)
+    return {
+        "workload": "cfg5: 256 seqs, ctx U[4096,32768], one layer, sequences LPT-sharded over the ranks",
+        "n_gpus": world, "per_rank_ms": per_rank, "imbalance_max_over_mean": slowest / (sum(per_rank) / len(per_rank)),
+        "ms": slowest, "value": total_bytes / (slowest * 1e-3) / 1e9, "unit": "GB/s",
+        "per_gpu_frac_of_hbm_peak": [b / (t * 1e-3) / 1e9 / peak for b, t in zip(per_rank_bytes, per_rank)],
+        "gather_ms": gather_ms, "gather_bytes": full.numel() * full.element_size(),
+        "gather_checksum_ok": bits_sum(full) == dp.sum_over_ranks(local_sum, dev),
+        "gather_backend": torch.distributed.get_backend() if world > 1 else "none (one rank)",
+    }
+
+
+def splitk_side(dlx, ops, dev, peak):
+    """A few long sequences (the first 8 of the scaling-sweep configuration: 32 work items for 74 CTA pairs), where
+    the planner cuts every sequence into key-range splits and the combine kernel merges them."""
+    from diffulex_b200.workload import make_problem, named_workload, small_workload
+    w5 = named_workload("cfg5")
+    g = w5.geometry
+    w = small_workload("cfg5_first8", g.num_q_heads, g.num_kv_heads, g.head_dim, g.page_size, g.diffusion_block_size,
+                       list(w5.context_lens[:8]), list(w5.new_lens[:8]), w5.mask_mode, w5.seed)
+    p = make_problem(w, device=dev, values="torch")
+    md = p.metadata("static")
+    splits = ops.planned_num_splits(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
+                                    p.cu_seqlens_q, p.cu_seqlens_k, p.scale, md.max_seqlen_q, 0, p.mask_mode,
+                                    g.diffusion_block_size, 0)
+    out = torch.empty_like(p.q)
+    fn = lambda: dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md, out=out)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(10):
+            fn()
+    graph.replay()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(3):
+        graph.replay()
+    eb.record()
+    torch.cuda.synchronize()
+    us = ea.elapsed_time(eb) / 30 * 1e3
+    gbps = p.kv_bytes() / (us * 1e-6) / 1e9
+    return {"workload": "8 sequences, ctx 4k..32k (cfg5's first 8), 28q/4kv x 128", "num_splits": splits,
+            "launches_per_call": 2 if splits > 1 else 1, "us_per_call": us, "gbps": gbps, "frac_of_peak": gbps / peak,
+            "kernels": "decode attention (key-range splits) + combine_splits"}
+
+
 def run_reference(args, w, rank, world):
     """The reference's CPU implementation of the path (its PyTorch attention check, restated in
     oracle/attn_oracle.py; the reference itself is Python and cannot travel) on the host cores."""
@@ -255,6 +368,7 @@ def main():
     assert torch.cuda.is_available(), "bench.py needs a CUDA device (there is no CPU fallback)"
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    pin_cpus(local_rank, world)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     import diffulex_b200 as dlx
@@ -282,6 +396,8 @@ def main():
     md = base.metadata("static")
     md.num_splits = args.num_splits
     kv_bytes_layer = base.kv_bytes()
+    kv_tokens_layer = int(base.host_context_lens.sum() + base.host_new_lens.sum())
+    query_block, seqs_per_gpu = int(base.host_new_lens.max()), base.num_seqs
     q_tokens = int(base.host_new_lens.sum())
     flops_layer = base.flops()
     splits = ops.planned_num_splits(base.q, base.k, base.v, base.k_cache, base.v_cache, base.block_tables,
@@ -369,6 +485,7 @@ def main():
 
     # ---- e2e: host buffers in, host buffers out, every step ----
     e2e = None
+    host_cost = None
     if not args.no_e2e:
         pin = lambda t: t.cpu().pin_memory()
         h_q = torch.stack([p.q for p in layers]).cpu().pin_memory()
@@ -382,55 +499,104 @@ def main():
         from types import SimpleNamespace
         h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, *h_meta.values()))
         d2h = h_out.numel() * h_out.element_size()
-
+        # Copies go in groups of layers: few, large transfers (one cudaMemcpyAsync per tensor per group), while the
+        # host->device copies of group g+1 and the device->host copy of group g-1 still run under the kernels of
+        # group g (three streams; PCIe is full duplex).
+        groups = [list(range(i, min(i + args.e2e_group, L))) for i in range(0, L, args.e2e_group)]
         s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        ev_in = [torch.cuda.Event() for _ in range(L)]
-        ev_c = [torch.cuda.Event() for _ in range(L)]
+        ev_in = [torch.cuda.Event() for _ in groups]
+        ev_c = [torch.cuda.Event() for _ in groups]
 
-        def e2e_step():
-            # Three streams: host->device copies of layer i+1 run under the kernels of layer i, and the
-            # device->host copy of layer i-1's output runs under them too (PCIe is full duplex).
+        def e2e_step(copies=True, kernels=True):
             cur = torch.cuda.current_stream()
             s_in.wait_stream(cur)
+            m = SimpleNamespace(**vars(md))
+            m.__dict__.pop("_dlx_schedule", None)      # a new step: the schedule is planned again from the copied metadata
             with torch.cuda.stream(s_in):
-                m = SimpleNamespace(**vars(md))
-                for n_, t in h_meta.items():
-                    setattr(m, n_, t.to(dev, non_blocking=True))
-                for i in range(L):
-                    d_q[i].copy_(h_q[i], non_blocking=True)
-                    d_k[i].copy_(h_k[i], non_blocking=True)
-                    d_v[i].copy_(h_v[i], non_blocking=True)
-                    ev_in[i].record(s_in)
-            for i, p in enumerate(layers):
-                cur.wait_event(ev_in[i])
-                dlx.store_kvcache_unified_layout(d_k[i], d_v[i], p.k_cache, p.v_cache, m.slot_mapping, m)
-                d_out[i] = dlx.dllm_flash_attn_decode(d_q[i], d_k[i], d_v[i], p.k_cache, p.v_cache, p.scale, m)
-                ev_c[i].record(cur)
-                s_out.wait_event(ev_c[i])
-                with torch.cuda.stream(s_out):
-                    h_out[i].copy_(d_out[i], non_blocking=True)
+                if copies:
+                    for n_, t in h_meta.items():
+                        setattr(m, n_, t.to(dev, non_blocking=True))
+                for gi, g in enumerate(groups):
+                    if copies:
+                        sl = slice(g[0], g[-1] + 1)
+                        d_q[sl].copy_(h_q[sl], non_blocking=True)
+                        d_k[sl].copy_(h_k[sl], non_blocking=True)
+                        d_v[sl].copy_(h_v[sl], non_blocking=True)
+                    ev_in[gi].record(s_in)
+            for gi, g in enumerate(groups):
+                cur.wait_event(ev_in[gi])
+                if kernels:
+                    for i in g:
+                        p = layers[i]
+                        dlx.store_kvcache_unified_layout(d_k[i], d_v[i], p.k_cache, p.v_cache, m.slot_mapping, m)
+                        dlx.dllm_flash_attn_decode(d_q[i], d_k[i], d_v[i], p.k_cache, p.v_cache, p.scale, m, out=d_out[i])
+                ev_c[gi].record(cur)
+                s_out.wait_event(ev_c[gi])
+                if copies:
+                    with torch.cuda.stream(s_out):
+                        sl = slice(g[0], g[-1] + 1)
+                        h_out[sl].copy_(d_out[sl], non_blocking=True)
             cur.wait_stream(s_out)
             cur.synchronize()  # the caller holds the result on the host
 
-        for _ in range(max(3, min(args.warmup, 5))):
-            e2e_step()
-        barrier()
-        e0.record()
-        n_e2e = max(3, min(args.steps, 10))
-        for _ in range(n_e2e):
-            e2e_step()
-        e1.record()
-        barrier()
-        ms_e2e = dp.max_over_ranks(e0.elapsed_time(e1), dev)
-        tot = dp.sum_over_ranks(float(kv_bytes_layer) * L * n_e2e, dev)
-        e2e = {"value": tot / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "steps": n_e2e, "ms_per_step": ms_e2e / n_e2e}
+        def timed_e2e(n, **kw):
+            for _ in range(2):
+                e2e_step(**kw)
+            barrier()
+            e0.record()
+            for _ in range(n):
+                e2e_step(**kw)
+            e1.record()
+            barrier()
+            return dp.max_over_ranks(e0.elapsed_time(e1), dev) / n
 
-    # ---- side measurement (rank 0, one GPU): store and load bandwidth on a cfg5-shaped layer ----
+        for _ in range(max(1, min(args.warmup, 3))):
+            e2e_step()
+        n_e2e = max(3, min(args.steps, 10))
+        ms_e2e = timed_e2e(n_e2e)
+        tot = dp.sum_over_ranks(float(kv_bytes_layer) * L, dev)
+        e2e = {"value": tot / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e, "ms_per_step": ms_e2e,
+               # the same step with the kernels left out (what the copies alone cost: PCIe / host memory ceiling) and
+               # with the copies left out (resident inputs through the same Python loop: launch cost + device time)
+               "copy_only_ms": timed_e2e(3, kernels=False), "launch_only_ms": timed_e2e(3, copies=False),
+               "layers_per_copy_group": args.e2e_group, "cpu_affinity": sorted(os.sched_getaffinity(0))[:4] + ["..."]}
+        e2e["host_link_gbps"] = (h2d + d2h) * world / (e2e["copy_only_ms"] * 1e-3) / 1e9   # all ranks, both directions
+
+        # host time per eager call (device-resident inputs): what a runner that never captures a graph pays per layer
+        p0 = layers[0]
+        m = SimpleNamespace(**vars(md))
+        def host_us(fn, n=300):
+            fn(); torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            dt = time.perf_counter() - t0
+            torch.cuda.synchronize()
+            return dt / n * 1e6
+        host_cost = {
+            "store_us": host_us(lambda: dlx.store_kvcache_unified_layout(p0.k, p0.v, p0.k_cache, p0.v_cache, m.slot_mapping, m)),
+            "decode_us": host_us(lambda: dlx.dllm_flash_attn_decode(p0.q, p0.k, p0.v, p0.k_cache, p0.v_cache, p0.scale, m,
+                                                                     out=d_out[0])),
+            "calls": 300, "note": "wall time per call of the Python entry point, launches queue on the device",
+        }
+
+    # ---- side measurements: the cfg2 state is released first ----
+    del layers, graph, g_dec, base
+    if e2e is not None:
+        del h_q, h_k, h_v, h_out, d_q, d_k, d_v, d_out
+    torch.cuda.empty_cache()
+    strong = None
+    if not args.no_strong:   # every rank takes part: sequences sharded over the ranks, outputs gathered
+        strong = strong_cfg5(dlx, dp, dev, rank, world, peak)
+        torch.cuda.empty_cache()
+    splitk = None
+    if rank == 0 and world == 1 and not args.no_splitk:
+        splitk = splitk_side(dlx, ops, dev, peak)
+        torch.cuda.empty_cache()
+    # store and load bandwidth on a cfg5-shaped layer (rank 0, one GPU)
     store_load = None
     if rank == 0 and world == 1 and not args.no_store_load:
-        del layers, graph, g_dec
-        torch.cuda.empty_cache()
         store_load = store_load_bandwidth(dlx, dev, peak, args.store_load_seqs)
 
     cpu = None
@@ -448,16 +614,18 @@ def main():
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "query_tokens_per_s": total_q_tokens / (ms_total * 1e-3),
-            "config": {"workload": f"{w_global.name}: {w_global.note}", "layers": L, "seqs_per_gpu": base.num_seqs,
+            "config": {"workload": f"{w_global.name}: {w_global.note}", "layers": L, "seqs_per_gpu": seqs_per_gpu,
                        "heads": f"{geo.num_q_heads}q/{geo.num_kv_heads}kv x {geo.head_dim}", "page_size": geo.page_size,
-                       "query_block": int(base.host_new_lens.max()), "kv_tokens_per_layer_per_gpu":
-                       int(base.host_context_lens.sum() + base.host_new_lens.sum()), "num_splits": splits,
+                       "query_block": query_block, "kv_tokens_per_layer_per_gpu":
+                       kv_tokens_layer, "num_splits": splits,
                        "step": "L x (store_kvcache_unified + decode attention), CUDA-graph replay",
                        "l2": f"inputs larger than L2: {L} distinct layer caches, "
                              f"{kv_bytes_layer * L / 1e9:.2f} GB of KV per step",
                        "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.scaling})")},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "store_load": store_load,
-            "gpu_launches": args.steps * L * launches_per_layer, "clocks": clocks, "per_rank_ms": per_rank_ms,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "host_us_per_call": host_cost,
+            "strong_cfg5": strong, "splitk": splitk, "store_load": store_load,
+            # per step: L x (store + decode [+ combine]) + the one planning launch of the step's schedule
+            "gpu_launches": args.steps * (L * launches_per_layer + 1), "clocks": clocks, "per_rank_ms": per_rank_ms,
         }
         print(json.dumps(line))
     if world > 1:

@@ -372,28 +372,31 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         m_ref = xm[slot * 128 + L];
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    if (u >= 1) {
-                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
-                        // this buffer must have been consumed before the next one goes in (and before this barrier's
-                        // next phase)
-                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                    }
                     // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
+                    // P = exp2(s * scale - m_ref) as bf16, a whole row in registers first: the exponentials do not need the
+                    // P buffer, only the stores at the end do, and by then the P V that last read the buffer has long run
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
+                    uint32_t pk[4][16];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t pk[16];
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                         }
-                        tmem_st16(tP + c * 16, pk);
                     }
+                    if (u >= 1) {
+                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in this
+                        // buffer must have been consumed before the next one goes in
+                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                        tc_fence_after();
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) tmem_st16(tP + c * 16, pk[c]);
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     const float tsum = lacc0.x + lacc0.y;
                     out_of_range |= !(tsum <= DLX_SUM_HIGH);   // exponent range left (also catches NaN): redo the item

@@ -68,13 +68,12 @@ static_assert(KSTAGES >= 2 && KSTAGES <= 4 && VSTAGES >= 2 && VSTAGES <= 4, "rin
 constexpr int OFF_K = 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * K_STAGE;
 constexpr int OFF_BAR = OFF_V + VSTAGES * V_STAGE;
-constexpr int OFF_TAB = OFF_BAR + 512;             // row-source pointer tables: one per loader warp, 128 rows
 constexpr int BT_SLOTS = 512;                      // page ids of a long item that its record does not hold
-constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;
+constexpr int OFF_BT = OFF_BAR + 512;
 constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 8 x 128 floats: row references and row sums between the warpgroups
-constexpr int OFF_STAGE = OFF_XCH + 8 * 128 * 4;   // output staging: 32 rows x 128 bytes per epilogue warp
+constexpr int OFF_STAGE = OFF_XCH + 8 * 128 * 4;   // output staging: 2 halves x 4 epilogue warps x (32 rows x 128 bytes)
 constexpr int STAGE_WARP_BYTES = 32 * 128;
-constexpr int OFF_ROWMAP = OFF_STAGE + 4 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group)
+constexpr int OFF_ROWMAP = OFF_STAGE + 8 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group)
 constexpr int MAX_ROUNDS = 32;                     // records kept in shared memory; later rounds are read from global
 constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;
 constexpr int OFF_FLAGS = OFF_ITEMS + MAX_ROUNDS * (int)sizeof(SchedRec);   // redo bit per round
@@ -114,9 +113,13 @@ static_assert(8 * B_COUNT + 16 <= 512, "barrier block");
 
 __device__ int g_status_pair[4];  // [0] bit 0: a bounded wait expired; [1] wait site, [2] tile, [3] CTA
 
+// Tensor maps of one launch, by level l = 0..7: boxes of 128 >> l rows x 64 head_dim columns.  kc / vc: the caches as
+// {head_dim, Hkv, page row, page}; kn / vn: the in-flight rows as {head_dim, Hkv, token}.  Levels whose box exceeds a
+// page (caches) are unused.  Any run of rows is a few boxes of falling size; a box may start at any row of a tile:
+// the 128-byte swizzle of a copy follows the shared-memory address it writes.
+constexpr int LEVELS = 8;
 struct TmaMapsPair {
-    CUtensorMap k[4];   // boxes of 64 >> level key rows x 64 head_dim columns
-    CUtensorMap v[5];   // boxes of 128 >> level key rows x 64 head_dim columns
+    CUtensorMap kc[LEVELS], vc[LEVELS], kn[LEVELS], vn[LEVELS];
     CUtensorMap q;
 };
 
@@ -334,25 +337,30 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                         m_ref = xm[slot * 128 + L];
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    if (u >= 1) {
-                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                        tc_fence_after();
-                    }
+                    // P = exp2(s * scale - m_ref) as bf16, a whole row in registers first: the exponentials do not need the
+                    // P buffer, only the stores at the end do, and by then the P V that last read the buffer has long run
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
+                    uint32_t pk[4][16];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t pk[16];
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                         }
-                        tmem_st16(tP + c * 16, pk);
                     }
+                    if (u >= 1) {
+                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in this
+                        // buffer must have been consumed before the next one goes in
+                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                        tc_fence_after();
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) tmem_st16(tP + c * 16, pk[c]);
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     const float tsum = lacc0.x + lacc0.y;
                     out_of_range |= !(tsum <= DLX_SUM_HIGH);   // also catches NaN
@@ -451,6 +459,9 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     atomicOr(&redo_flags[(round >> 5) & (FLAG_WORDS - 1)], 1u << (round & 31));
                 const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
                 if (a.num_splits == 1) {
+                    // bf16 output.  Both halves of O (64 head_dim columns each) go to a swizzled staging buffer first, and O is
+                    // released to the next item's P V right after the second load; the rows then leave as 4 rows x 128
+                    // contiguous bytes per store instruction (a thread holds a ROW: direct stores would touch 32 lines).
 #pragma unroll 1
                     for (int c = 0; c < 2; ++c) {
                         uint32_t v[2][32];
@@ -462,6 +473,7 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                             __syncwarp();
                             if (lane == 0) mbar_arrive_cluster(bar0(B_OFREE));   // the next item's P V may overwrite O
                         }
+                        unsigned char* st = stage + c * (4 * STAGE_WARP_BYTES);
 #pragma unroll
                         for (int q4 = 0; q4 < 8; ++q4) {
                             const uint32_t* x = &v[q4 >> 2][(q4 & 3) * 8];
@@ -470,22 +482,25 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                             o.y = pack2<__nv_bfloat16>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv);
                             o.z = pack2<__nv_bfloat16>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv);
                             o.w = pack2<__nv_bfloat16>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv);
-                            *reinterpret_cast<uint4*>(stage + lane * 128 + ((q4 ^ (lane & 7)) << 4)) = o;
+                            *reinterpret_cast<uint4*>(st + lane * 128 + ((q4 ^ (lane & 7)) << 4)) = o;
                         }
-                        __syncwarp();
-#pragma unroll 2
-                        for (int i = 0; i < 8; ++i) {
-                            const int row = 4 * i + (lane >> 3);
-                            const int R = wq * 32 + row;
-                            const uint4 o = *reinterpret_cast<const uint4*>(stage + row * 128 + (((lane & 7) ^ (row & 7)) << 4));
-                            if (R < rows_here) {
-                                const int2 dm = rowmap[R];
-                                char* dst = static_cast<char*>(a.out) + (((int64_t)(it.q0 + it.tok0 + dm.x) * a.o_rs + (int64_t)(head0 + dm.y) * HD) << 1);
-                                *reinterpret_cast<uint4*>(dst + c * 128 + (lane & 7) * 16) = o;
-                            }
-                        }
-                        __syncwarp();
                     }
+                    __syncwarp();
+#pragma unroll 1
+                    for (int i = 0; i < 8; ++i) {
+                        const int row = 4 * i + (lane >> 3);
+                        const int R = wq * 32 + row;
+                        if (R < rows_here) {
+                            const int2 dm = rowmap[R];
+                            char* dst = static_cast<char*>(a.out) + (((int64_t)(it.q0 + it.tok0 + dm.x) * a.o_rs + (int64_t)(head0 + dm.y) * HD) << 1);
+                            const uint32_t so = row * 128 + (((lane & 7) ^ (row & 7)) << 4);
+                            const uint4 o0 = *reinterpret_cast<const uint4*>(stage + so);
+                            const uint4 o1 = *reinterpret_cast<const uint4*>(stage + 4 * STAGE_WARP_BYTES + so);
+                            *reinterpret_cast<uint4*>(dst + (lane & 7) * 16) = o0;
+                            *reinterpret_cast<uint4*>(dst + 128 + (lane & 7) * 16) = o1;
+                        }
+                    }
+                    __syncwarp();
                 } else {
                     const int2 my_row = rowmap[L];
                     const int64_t tok = it.q0 + it.tok0 + (row_valid ? my_row.x : 0);
@@ -527,20 +542,14 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
         // ring position and page are tracked incrementally, the page id comes from the record.  Every other tile
         // (the end of the prefix, in-flight rows, small pages) takes the general path with the whole warp.
         const int which = warp == VLOAD_WARP;
-        const char* qp = static_cast<const char*>(a.q);
-        const char* cache = static_cast<const char*>(which ? a.v_cache : a.k_cache);
-        const char* fresh = static_cast<const char*>(which ? a.v : a.k);
-        const int64_t fresh_rs = which ? a.v_rs : a.k_rs;
         int32_t* bt_base = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
-        const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
         const int stages = which ? VSTAGES : KSTAGES;
         const int row_lo = which ? 0 : K_ROWS * rank;          // first tile row this loader fetches
         const int rows_mine = which ? TILE_N : K_ROWS;
-        const int col_byte0 = which ? 128 * rank : 0;          // first byte of a key row this loader fetches
         const int c0_tma = which ? 64 * rank : 0;              // first head_dim column of its boxes
         const int box_rows0 = which ? a.tma_box_rows : min(a.tma_box_rows, K_ROWS);
-        const int lvl0 = which ? a.tma_lvl0 : max(a.tma_lvl0 - 1, 0);   // K levels count from 64 rows, V from 128
-        const CUtensorMap* lvl_maps = which ? maps.v : maps.k;
+        const int lvl0 = which ? a.tma_lvl0 : max(a.tma_lvl0, 1);   // level of the largest cache box this loader uses
+        const CUtensorMap* lvl_maps = which ? maps.vc : maps.kc;
         const int page_size = a.page_size;
         const bool one_box_geom = box_rows0 == rows_mine && page_size % TILE_N == 0;   // a whole tile part is one box (pair)
         const int tiles_per_page = page_size / TILE_N;         // used only with one_box_geom
@@ -602,110 +611,68 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                         if (ok) {
                             mbar_arrive_expect_tx(full, stage_bytes);
                             if (which) {
-                                tma_load_4d(d0, &lvl_maps[0], c0_tma, kvh, prow, pid0, full);
+                                tma_load_4d(d0, &lvl_maps[lvl0], c0_tma, kvh, prow, pid0, full);
                             } else {
-                                tma_load_4d(d0, &lvl_maps[0], 0, kvh, prow, pid0, full);
-                                tma_load_4d(d0 + K_REGION, &lvl_maps[0], 64, kvh, prow, pid0, full);
+                                tma_load_4d(d0, &lvl_maps[lvl0], 0, kvh, prow, pid0, full);
+                                tma_load_4d(d0 + K_REGION, &lvl_maps[lvl0], 64, kvh, prow, pid0, full);
                             }
                         }
                     }
                     early_ready = __shfl_sync(0xffffffffu, (int)early_ready, 0) != 0;
                     alive = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
                 } else {
-                    // ---- general path (whole warp): the tile with the end of the prefix, in-flight rows, small pages ----
-                    const bool by_tma = p0 + rows_mine <= ctx;
-                    int tma_rows = 0, c_end = rows_mine;
-                    if (!by_tma) {
-                        tma_rows = max(min(ctx - p0, rows_mine), 0) & ~7;
-                        c_end = max(min(it.total - p0, rows_mine), 0);
-                    }
-                    int pjg = p0 / page_size, prow = p0 - pjg * page_size;
-                    if (!early_ready && pjg < early) {
-                        asm volatile("cp.async.wait_all;\n" ::: "memory");
-                        __syncwarp();
-                        early_ready = true;
-                    }
-                    if (!by_tma) {
-                        int pj2 = pjg, prow2 = prow + tma_rows;
-                        if (prow2 >= page_size) { pj2 += prow2 / page_size; prow2 %= page_size; }
-                        const int64_t pid2 = (int64_t)page_id(pj2);
-#pragma unroll 1
-                        for (int hh = 0; hh < 4; ++hh) {
-                            const int row = tma_rows + lane + 32 * hh;
-                            if (row >= c_end) break;
-                            const int p = p0 + row;
-                            const char* ptr = nullptr;
-                            if (p < ctx) {   // the cached rows left over after the boxes: fewer than 8, all in one page
-                                if (pid2 >= 0 && pid2 < a.num_pages)
-                                    ptr = cache + ((pid2 * a.page_stride + (int64_t)(prow2 + row - tma_rows) * a.token_stride + kvh * HD) << 1);
-                            } else if (p < it.total) {
-                                ptr = fresh + (((int64_t)(it.kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
-                            }
-                            tab[row] = ptr;
-                        }
-                        __syncwarp();
-                    }
-                    bool ok = mbar_wait(bar_empty0 + 8u * stage, par_empty, abort_flag, 5 + which, jj);
-                    if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                    if (!by_tma) {
-                        // Rows by 16-byte cp.async.  Each lane's arrival is tied to its own copies and adds itself to the
-                        // barrier's pending count first, so the one counted arrival (lane 0, below) closes the phase only
-                        // when every copy has landed.
-                        if (which) {
-                            // V: 128 bytes (this CTA's 64 columns) per row, 8 chunks; 4 rows per pass
-                            const int col = lane & 7, rb = lane >> 3;
-                            const int passes = (c_end - tma_rows + 3) >> 2;
-#pragma unroll 2
-                            for (int i = 0; i < passes; ++i) {
-                                const int row = tma_rows + rb + 4 * i;
-                                if (row < c_end) {
-                                    const char* rp = tab[row];
-                                    cp_async_16(d0 + row * 128 + ((col ^ (row & 7)) << 4), rp ? rp + col_byte0 + col * 16 : qp, rp ? 16 : 0);
-                                }
-                            }
-                        } else {
-                            // K: 256 bytes per row, 16 chunks over two regions; 2 rows per pass
-                            const int col = lane & 15, rb = lane >> 4;
-                            const uint32_t dbase = d0 + (col >> 3) * K_REGION;
-                            const int c8 = col & 7;
-                            const int passes = (c_end - tma_rows + 1) >> 1;
-#pragma unroll 2
-                            for (int i = 0; i < passes; ++i) {
-                                const int row = tma_rows + rb + 2 * i;
-                                if (row < c_end) {
-                                    const char* rp = tab[row];
-                                    cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
-                                }
-                            }
-                        }
-                        asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];\n" ::"r"(full) : "memory");
-                        __syncwarp();   // every lane is on the pending count before lane 0 arrives; the table may be rebuilt
-                    }
+                    // ---- general path: the tile with the end of the prefix, in-flight rows, small pages.  Lane 0 cuts the
+                    // cached rows and the in-flight rows of its part into boxes of falling size (128 >> level rows) ----
+                    bool ok = true;
                     if (lane == 0) {
-                        const int rows_by_tma = by_tma ? rows_mine : tma_rows;
-                        if (rows_by_tma > 0) {
-                            mbar_arrive_expect_tx(full, (uint32_t)rows_by_tma * (which ? 128u : 256u));
-                            int r0 = 0;
-                            int lvl = lvl0;
+                        const int cr = max(min(ctx - p0, rows_mine), 0);        // cached rows of this part
+                        const int ce = max(min(it.total - p0, rows_mine), 0);   // ... plus in-flight rows; the rest stays as it is
+                        int pjg = p0 / page_size, prow = p0 - pjg * page_size;
+                        if (!early_ready && pjg < early && cr > 0) {
+                            asm volatile("cp.async.wait_all;\n" ::: "memory");
+                            early_ready = true;
+                        }
+                        ok = mbar_wait(bar_empty0 + 8u * stage, par_empty, abort_flag, 5 + which, jj);
+                        if (ok) {
+                            if (ce == 0) {
+                                mbar_arrive(full);
+                            } else {
+                                mbar_arrive_expect_tx(full, (uint32_t)ce * (which ? 128u : 256u));
+                                int r = 0;
+                                int lvl = lvl0;
 #pragma unroll 1
-                            for (int sz = box_rows0; sz >= 8; sz >>= 1, ++lvl) {
-                                while (rows_by_tma - r0 >= sz) {
-                                    const int pid = page_id(pjg);   // a bad id is out of bounds: zero fill
-                                    if (which) {
-                                        tma_load_4d(d0 + r0 * 128, &lvl_maps[lvl], c0_tma, kvh, prow, pid, full);
-                                    } else {
-                                        tma_load_4d(d0 + r0 * 128, &lvl_maps[lvl], 0, kvh, prow, pid, full);
-                                        tma_load_4d(d0 + K_REGION + r0 * 128, &lvl_maps[lvl], 64, kvh, prow, pid, full);
+                                for (int sz = box_rows0; sz >= 1; sz >>= 1, ++lvl) {
+                                    while (cr - r >= sz) {
+                                        const int pid = page_id(pjg);   // a bad id is out of bounds: zero fill
+                                        if (which) {
+                                            tma_load_4d(d0 + r * 128, &maps.vc[lvl], c0_tma, kvh, prow, pid, full);
+                                        } else {
+                                            tma_load_4d(d0 + r * 128, &maps.kc[lvl], 0, kvh, prow, pid, full);
+                                            tma_load_4d(d0 + K_REGION + r * 128, &maps.kc[lvl], 64, kvh, prow, pid, full);
+                                        }
+                                        r += sz; prow += sz;
+                                        if (prow >= page_size) { prow = 0; ++pjg; }   // boxes never straddle a page
                                     }
-                                    r0 += sz; prow += sz;
-                                    if (prow >= page_size) { prow = 0; ++pjg; }   // boxes never straddle a page
+                                }
+                                int tok = it.kv0 + (p0 + cr - ctx);   // first in-flight row of this part
+                                lvl = which ? 0 : 1;
+#pragma unroll 1
+                                for (int sz = rows_mine; sz >= 1; sz >>= 1, ++lvl) {
+                                    while (ce - r >= sz) {
+                                        if (which) {
+                                            tma_load_3d(d0 + r * 128, &maps.vn[lvl], c0_tma, kvh, tok, full);
+                                        } else {
+                                            tma_load_3d(d0 + r * 128, &maps.kn[lvl], 0, kvh, tok, full);
+                                            tma_load_3d(d0 + K_REGION + r * 128, &maps.kn[lvl], 64, kvh, tok, full);
+                                        }
+                                        r += sz; tok += sz;
+                                    }
                                 }
                             }
-                        } else {
-                            mbar_arrive(full);
                         }
                     }
-                    __syncwarp();
+                    early_ready = __shfl_sync(0xffffffffu, (int)early_ready, 0) != 0;
+                    alive = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
                 }
                 if (++stage == stages) { stage = 0; par_empty ^= 1u; }
             }
@@ -900,17 +867,22 @@ int launch_decode_tc5_pair(const DecodeArgs& a_in, cudaStream_t st) {
     const bool fits = a.max_blocks > 0 && a.num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
     const bool strides_ok = a.token_stride * 2 % 16 == 0 && a.page_stride * 2 % 16 == 0 &&
                             a.page_stride * 2 < (1ll << 40) && a.num_pages < (1ll << 31);
-    if (!fits || !strides_ok || a.total_q <= 0 || a.q_rs * 2 % 16 != 0 || a.q_rs * 2 >= (1ll << 40))
+    if (!fits || !strides_ok || a.total_q <= 0 || a.q_rs * 2 % 16 != 0 || a.q_rs * 2 >= (1ll << 40) ||
+        a.k_rs * 2 % 16 != 0 || a.v_rs * 2 % 16 != 0 || a.k_rs * 2 >= (1ll << 40) || a.v_rs * 2 >= (1ll << 40))
         return fail(DLX_ERR_UNSUPPORTED, "decode (pair kernel): page size %d or strides not served", ps);
     a.tma_box_rows = ps < 128 ? ps : 128;
     a.tma_lvl0 = 0;
     while ((128 >> a.tma_lvl0) > a.tma_box_rows) ++a.tma_lvl0;
-    for (int lvl = a.tma_lvl0; lvl < 5; ++lvl) {   // V: boxes of 128 >> lvl rows
-        const int rc = tc5::tc5_cache_map(a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 128 >> lvl, 4, &maps.v[lvl]);
-        if (rc != DLX_OK) return rc;
-    }
-    for (int lvl = (a.tma_lvl0 > 0 ? a.tma_lvl0 - 1 : 0); lvl < 4; ++lvl) {   // K: boxes of 64 >> lvl rows
-        const int rc = tc5::tc5_cache_map(a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 64 >> lvl, 4, &maps.k[lvl]);
+    for (int lvl = 0; lvl < tc5p::LEVELS; ++lvl) {
+        const int rows = 128 >> lvl;
+        int rc = DLX_OK;
+        if (rows <= ps) {   // caches: a box lies inside one page
+            rc = tc5::tc5_cache_map(a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows, 4, &maps.kc[lvl]);
+            if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows, 4, &maps.vc[lvl]);
+        }
+        // in-flight rows: {head_dim, Hkv, token}, box {64, 1, rows}
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.k, a.k_rs, 0, a.total_q, a.hkv, 1, rows, 3, &maps.kn[lvl]);
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v, a.v_rs, 0, a.total_q, a.hkv, 1, rows, 3, &maps.vn[lvl]);
         if (rc != DLX_OK) return rc;
     }
     {

@@ -121,6 +121,65 @@ store_distinct_kernel(const E* __restrict__ key, int64_t key_row_stride, const E
     }
 }
 
+// Fast form for x = 8 two-byte elements (one 16-byte vector per (head, dx, token)) and 16-byte aligned rows: a CTA
+// takes 32 consecutive tokens and walks the row in chunks of 512 elements through shared memory.  Lanes are TOKENS:
+// for a fixed (head, dx) the K vectors of tokens that sit in consecutive slots of one page are 32 x 16 contiguous
+// bytes, and for a fixed (head, d) their V elements are 32 x 2 contiguous bytes, so a block of tokens stored to
+// consecutive slots leaves as whole lines instead of 2-byte pieces strided by the page size.
+constexpr int kDistTokens = 32, kDistChunk = 512;
+template <typename SlotT>
+__global__ void __launch_bounds__(256)
+store_distinct_x8_kernel(const uint16_t* __restrict__ key, int64_t key_row_stride, const uint16_t* __restrict__ value,
+                         int64_t value_row_stride, uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache,
+                         const SlotT* __restrict__ slots, int64_t num_tokens, int heads, int hd, int page,
+                         int64_t num_pages) {
+    constexpr int KROW = kDistChunk * 2 + 16;   // bytes per token in the K tile: vectors stay aligned, quarter-warps conflict-free
+    constexpr int VROW = kDistChunk * 2 + 4;    // bytes per token in the V tile: an odd number of words, columns conflict-free
+    __shared__ __align__(16) unsigned char tile[kDistTokens * KROW];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t t0 = (int64_t)blockIdx.x * kDistTokens;
+    const int D = heads * hd;
+    // this lane's token
+    const int64_t t = t0 + lane;
+    int64_t slot = -1;
+    if (t < num_tokens) slot = (int64_t)slots[t];
+    const bool live = slot >= 0 && slot < num_pages * page;
+    const int64_t b = live ? slot / page : 0;
+    const int off = live ? (int)(slot - b * page) : 0;
+    for (int c0 = 0; c0 < D; c0 += kDistChunk) {
+        const int cw = min(kDistChunk, D - c0);           // elements of this chunk (a multiple of 8)
+        // ---- K: rows -> shared (16-byte vectors, coalesced), then one vector per (token, head, dx) ----
+        __syncthreads();
+        for (int i = tid; i < kDistTokens * (cw >> 3); i += 256) {
+            const int r = i / (cw >> 3), v = i - r * (cw >> 3);
+            uint4 x = make_uint4(0, 0, 0, 0);
+            if (t0 + r < num_tokens) x = *reinterpret_cast<const uint4*>(key + (t0 + r) * key_row_stride + c0 + v * 8);
+            *reinterpret_cast<uint4*>(tile + r * KROW + v * 16) = x;
+        }
+        __syncthreads();
+        if (live)
+            for (int g = warp; g < (cw >> 3); g += 8) {
+                const int e = c0 + g * 8, h = e / hd, dx = (e - h * hd) >> 3;
+                const uint4 x = *reinterpret_cast<const uint4*>(tile + lane * KROW + g * 16);
+                *reinterpret_cast<uint4*>(k_cache + ((((b * heads + h) * (hd >> 3) + dx) * page + off) << 3)) = x;
+            }
+        // ---- V: rows -> shared (4-byte words), then one element per (token, head, d) ----
+        __syncthreads();
+        for (int i = tid; i < kDistTokens * (cw >> 1); i += 256) {
+            const int r = i / (cw >> 1), v = i - r * (cw >> 1);
+            uint32_t x = 0;
+            if (t0 + r < num_tokens) x = *reinterpret_cast<const uint32_t*>(value + (t0 + r) * value_row_stride + c0 + v * 2);
+            *reinterpret_cast<uint32_t*>(tile + r * VROW + v * 4) = x;
+        }
+        __syncthreads();
+        if (live)
+            for (int c = warp; c < cw; c += 8) {
+                const int e = c0 + c, h = e / hd, d = e - h * hd;
+                v_cache[((b * heads + h) * hd + d) * page + off] = *reinterpret_cast<const uint16_t*>(tile + lane * VROW + c * 2);
+            }
+    }
+}
+
 // ---- load (gather) --------------------------------------------------------------------------
 // A CTA owns ROWS consecutive output rows.  The first ROWS threads resolve, per row, the owning
 // sequence (binary search in cu_seqlens_k) and the source row (cache page through the block table,
@@ -228,8 +287,21 @@ extern "C" int dlx_store_kvcache_distinct(const void* key, int64_t key_row_strid
         return fail(DLX_ERR_INVALID_ARGUMENT, "store_distinct: null pointer");
     if (num_tokens > 0x7fffffffLL) return fail(DLX_ERR_UNSUPPORTED, "store_distinct: more than 2^31-1 tokens");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    dim3 grid((unsigned)num_tokens), block(128);
     using E = uint16_t;
+    if (x == 8 && aligned16(key) && aligned16(value) && aligned16(k_cache) && key_row_stride % 8 == 0 &&
+        value_row_stride % 8 == 0) {
+        dim3 grid((unsigned)((num_tokens + kDistTokens - 1) / kDistTokens)), block(256);
+        if (slot_is_int64)
+            store_distinct_x8_kernel<int64_t><<<grid, block, 0, st>>>(
+                (const E*)key, key_row_stride, (const E*)value, value_row_stride, (E*)k_cache, (E*)v_cache,
+                (const int64_t*)slot_mapping, num_tokens, num_kv_heads, head_dim, page_size, num_pages);
+        else
+            store_distinct_x8_kernel<int32_t><<<grid, block, 0, st>>>(
+                (const E*)key, key_row_stride, (const E*)value, value_row_stride, (E*)k_cache, (E*)v_cache,
+                (const int32_t*)slot_mapping, num_tokens, num_kv_heads, head_dim, page_size, num_pages);
+        return check_launch("store_distinct_x8_kernel");
+    }
+    dim3 grid((unsigned)num_tokens), block(128);
     if (slot_is_int64)
         store_distinct_kernel<int64_t, E><<<grid, block, 0, st>>>(
             (const E*)key, key_row_stride, (const E*)value, value_row_stride, (E*)k_cache, (E*)v_cache,

@@ -120,6 +120,20 @@ def store_inputs(case: dict):
     return key, value, p.k_cache, p.v_cache, slots
 
 
+DISTINCT_X = 8   # elements of head_dim kept together in the split K layout (Config.k_cache_hdim_split_factor_x)
+
+
+def distinct_caches(case: dict):
+    """Seeded caches in the split ("distinct") layout for a store case: K ``[NB, H, hd/x, PAGE, x]``, V ``[NB, H, hd,
+    PAGE]`` (diffulex_kernel/python/kv_cache_kernels.py:86-91), bf16, same page count and geometry as the case's
+    unified caches."""
+    _, _, k_cache, _, _ = store_inputs(case)
+    nb, page, h, hd = k_cache.shape
+    rng = np.random.default_rng([case["w"]().seed, 99])
+    mk = lambda shape: torch.from_numpy(rng.standard_normal(size=shape, dtype=np.float32)).to(torch.bfloat16)
+    return mk((nb, h, hd // DISTINCT_X, page, DISTINCT_X)), mk((nb, h, hd, page))
+
+
 # ---- load --------------------------------------------------------------------------------------
 LOAD_CASES = {
     # page-aligned contexts 256 and 512: the reference leaves their last page unwritten

@@ -5,8 +5,9 @@ Usage (in a container that has the reference checkout; it is not needed to run t
     python tests/golden/make_golden.py /path/to/Diffulex
 
 What is run, unmodified, from the reference checkout:
-  * store: ``store_kvcache_unified_layout`` (diffulex_kernel/python/kv_cache_kernels.py:110-124),
-    its Triton kernel executed by the Triton interpreter (TRITON_INTERPRET=1) on CPU tensors;
+  * store: ``store_kvcache_unified_layout`` (diffulex_kernel/python/kv_cache_kernels.py:110-124) and
+    ``store_kvcache_distinct_layout`` (:86-107), their Triton kernels executed by the Triton interpreter
+    (TRITON_INTERPRET=1) on CPU tensors;
   * load: ``load_kvcache`` (kv_cache_kernels.py:230-279), same way;
   * attention: ``naive_sdpa_with_kvcache`` (tests/python/kernel/
     test_dllm_flash_attn_decode_kernel.py:14-105) in fp32 on CPU, and for the block-causal
@@ -15,7 +16,7 @@ What is run, unmodified, from the reference checkout:
 bf16 tensors are handed to the Triton interpreter as their int16 bit patterns (a copy is a
 copy); attention inputs are the bf16-rounded values widened to fp32.
 
-Outputs: store_golden.json / load_golden.json (sha256 digests: bit-exact work needs no more),
+Outputs: store_golden.json / store_distinct_golden.json / load_golden.json (sha256 digests: bit-exact work needs no more),
 load_written_rows.npz (which rows the reference wrote), attn_golden.npz (fp32 outputs of a few
 heads per case).
 """
@@ -36,7 +37,7 @@ import numpy as np
 import torch
 
 from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, attn_problem, bits, digest,
-                                load_problem, store_inputs)
+                                distinct_caches, load_problem, store_inputs)
 
 SENTINEL = 1  # int16 bit pattern of a bf16 denormal; N(0,1) draws rounded to bf16 never produce it
 
@@ -55,6 +56,19 @@ def gen_store(ref_kv):
         out[name] = dict(inputs=in_digest, k_cache=digest(kc), v_cache=digest(vc))
         print("store", name, out[name]["k_cache"][:12])
     (HERE / "store_golden.json").write_text(json.dumps(out, indent=1))
+
+
+def gen_store_distinct(ref_kv):
+    out = {}
+    for name, case in STORE_CASES.items():
+        key, value, _, _, slots = store_inputs(case)
+        k_cache, v_cache = distinct_caches(case)
+        in_digest = digest(key.contiguous(), value.contiguous(), k_cache, v_cache, slots)
+        kc, vc = as_i16(k_cache).clone(), as_i16(v_cache).clone()
+        ref_kv.store_kvcache_distinct_layout(as_i16(key), as_i16(value), kc, vc, slots, None)
+        out[name] = dict(inputs=in_digest, k_cache=digest(kc), v_cache=digest(vc))
+        print("store distinct", name, out[name]["k_cache"][:12])
+    (HERE / "store_distinct_golden.json").write_text(json.dumps(out, indent=1))
 
 
 def gen_load(ref_kv):
@@ -134,6 +148,7 @@ def main():
     sys.path.insert(0, str(ref_root / "tests" / "python" / "kernel"))
     import diffulex_kernel.python.kv_cache_kernels as ref_kv
     gen_store(ref_kv)
+    gen_store_distinct(ref_kv)
     gen_load(ref_kv)
     import test_dllm_flash_attn_decode_kernel as ref_decode_test
     import test_dllm_flash_attn_prefill_kernel as ref_prefill_test

@@ -246,3 +246,51 @@ def test_dp_gather_world_size_2_gloo():
         assert p.exitcode == 0
     for rank, ok, t, ts, tot in results:
         assert ok and t == 2.0 and ts == [1.0, 2.0] and tot == 20.0
+
+
+# ---- a rank that leaves between steps -------------------------------------------------------------
+def _leaving_worker(rank, world_size, port, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world_size, timeout=datetime.timedelta(seconds=8))
+    from diffulex_b200 import dp
+    q_lens, parts = [2, 3], [[0], [1]]
+    local = torch.full((q_lens[rank], 1, 4), float(rank))
+    full = dp.gather_outputs(local, parts, q_lens)            # step 1: both ranks are there
+    first_ok = full.shape[0] == 5 and float(full[:, 0, 0].sum()) == 3.0
+    if rank == 1:
+        q.put((rank, first_ok, "left"))
+        q.close(); q.join_thread()
+        os._exit(0)                                           # leaves between steps, nothing in flight
+    time.sleep(1.0)
+    t0 = time.time()
+    try:
+        dp.gather_outputs(local, parts, q_lens)               # step 2: the peer is gone
+        outcome = "no error"
+    except Exception as e:   # the process group reports the missing rank (closed connection or timeout)
+        outcome = type(e).__name__
+    q.put((rank, first_ok, outcome, time.time() - t0))
+    q.close(); q.join_thread()
+    os._exit(0)   # the group cannot be torn down cleanly without its peer
+
+
+def test_gather_reports_a_rank_that_left_instead_of_hanging():
+    """Failure detection on the host: a data-parallel rank exits between two steps; the survivor's next output
+    gather raises within the process group's (short) timeout instead of waiting forever."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        item = q.get(timeout=90)
+        got[item[0]] = item
+    for p in procs:
+        p.join(timeout=30)
+    assert got[1][1] and got[1][2] == "left"
+    assert got[0][1], "the first gather (both ranks present) must work"
+    assert got[0][2] != "no error", "the second gather must fail once the peer is gone"
+    assert got[0][3] < 60.0

@@ -72,17 +72,29 @@ def test_store_bit_exact(name, dlx, golden_dir):
     assert digest(kc.cpu()) == golden["k_cache"] and digest(vc.cpu()) == golden["v_cache"]
 
 
-def test_store_distinct_layout_bit_exact(dlx):
-    key, value, k_cache, v_cache, slots = store_inputs(STORE_CASES["neg_slots_int64"])
-    nb, page, h, hd = k_cache.shape
-    x = 8
-    kc = torch.randn(nb, h, hd // x, page, x).to(torch.bfloat16)
-    vc = torch.randn(nb, h, hd, page).to(torch.bfloat16)
+@pytest.mark.parametrize("name", list(STORE_CASES))
+def test_store_distinct_layout_bit_exact(name, dlx, golden_dir):
+    """Split layout (K [NB, H, hd/x, PAGE, x], V [NB, H, hd, PAGE]): bit-exact against the oracle and against the
+    digests of what the reference's own kernel wrote; int32 and int64 slots, skipped rows, strided key rows."""
+    from tests.golden.cases import distinct_caches
+    golden = json.loads((golden_dir / "store_distinct_golden.json").read_text())[name]
+    key, value, _, _, slots = store_inputs(STORE_CASES[name])
+    kc, vc = distinct_caches(STORE_CASES[name])
     kc_ref, vc_ref = bits(kc).copy(), bits(vc).copy()
     kv_cache_oracle.store_kvcache_distinct(bits(key), bits(value), kc_ref, vc_ref, slots.numpy())
+    kd, vd = key.cuda(), value.cuda()
+    if not key.is_contiguous():  # keep the row padding on the device too
+        n, h, d = key.shape
+        wide_k = torch.zeros(n, key.stride(0), dtype=key.dtype, device="cuda")
+        wide_v = torch.zeros_like(wide_k)
+        wide_k[:, : h * d] = key.reshape(n, -1).cuda()
+        wide_v[:, : h * d] = value.reshape(n, -1).cuda()
+        kd, vd = wide_k[:, : h * d].view(n, h, d), wide_v[:, : h * d].view(n, h, d)
     kcd, vcd = kc.cuda(), vc.cuda()
-    dlx.store_kvcache_distinct_layout(key.cuda(), value.cuda(), kcd, vcd, slots.cuda(), None)
+    assert dlx.store_kvcache_distinct_layout(kd, vd, kcd, vcd, slots.cuda(), None) is None
+    torch.cuda.synchronize()
     assert np.array_equal(bits(kcd), kc_ref) and np.array_equal(bits(vcd), vc_ref)
+    assert digest(kcd.cpu()) == golden["k_cache"] and digest(vcd.cpu()) == golden["v_cache"]
 
 
 # ---- load --------------------------------------------------------------------------------------

@@ -8,7 +8,7 @@ import torch
 
 from oracle import attn_oracle, kv_cache_oracle
 from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, attn_problem, bits, digest,
-                                load_problem, store_inputs)
+                                distinct_caches, load_problem, store_inputs)
 
 
 @pytest.fixture(scope="module")
@@ -33,6 +33,19 @@ def test_store_oracle_matches_reference(name, store_golden):
     assert digest(key.contiguous(), value.contiguous(), k_cache, v_cache, slots) == g["inputs"], "inputs drifted"
     kc, vc = bits(k_cache).copy(), bits(v_cache).copy()
     kv_cache_oracle.store_kvcache_unified(bits(key), bits(value), kc, vc, slots.numpy())
+    assert digest(kc) == g["k_cache"]
+    assert digest(vc) == g["v_cache"]
+
+
+@pytest.mark.parametrize("name", list(STORE_CASES))
+def test_distinct_store_oracle_matches_reference(name, golden_dir):
+    """The split-layout store oracle against what the reference's own Triton kernel wrote (interpreter run)."""
+    g = json.loads((golden_dir / "store_distinct_golden.json").read_text())[name]
+    key, value, _, _, slots = store_inputs(STORE_CASES[name])
+    k_cache, v_cache = distinct_caches(STORE_CASES[name])
+    assert digest(key.contiguous(), value.contiguous(), k_cache, v_cache, slots) == g["inputs"], "inputs drifted"
+    kc, vc = bits(k_cache).copy(), bits(v_cache).copy()
+    kv_cache_oracle.store_kvcache_distinct(bits(key), bits(value), kc, vc, slots.numpy())
     assert digest(kc) == g["k_cache"]
     assert digest(vc) == g["v_cache"]
 
