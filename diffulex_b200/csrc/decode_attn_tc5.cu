@@ -373,30 +373,37 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
                     // P = exp2(s*scale - m_ref) as bf16 into this warpgroup's P buffer
-                    // P = exp2(s * scale - m_ref) as bf16, a whole row in registers first: the exponentials do not need the
-                    // P buffer, only the stores at the end do, and by then the P V that last read the buffer has long run
+                    // P = exp2(s * scale - m_ref) as bf16.  The first half of the row is kept in registers: the exponentials
+                    // do not need the P buffer, only the stores do, and half a row later the P V that last read the
+                    // buffer has run (waiting for it up front would stall here, a whole row in registers costs too many)
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
-                    uint32_t pk[4][16];
+                    uint32_t pk[2][16];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
+                        uint32_t pc[16];
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            if (c < 2) pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y); else pc[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                        }
+                        if (c == 1) {
+                            if (u >= 1) {
+                                // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
+                                // this buffer must have been consumed before the next one goes in
+                                bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                                if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                                tc_fence_after();
+                            }
+                            tmem_st16(tP, pk[0]);
+                            tmem_st16(tP + 16, pk[1]);
+                        } else if (c >= 2) {
+                            tmem_st16(tP + c * 16, pc);
                         }
                     }
-                    if (u >= 1) {
-                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in this
-                        // buffer must have been consumed before the next one goes in
-                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                        tc_fence_after();
-                    }
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tmem_st16(tP + c * 16, pk[c]);
+                    if (!alive) break;
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     const float tsum = lacc0.x + lacc0.y;
                     out_of_range |= !(tsum <= DLX_SUM_HIGH);   // exponent range left (also catches NaN): redo the item

@@ -181,24 +181,21 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
     const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);   // for use AFTER the set-up barrier
     const int G = a_param.group;
 
-    if (tid == 0) {
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(B_QFULL + s), 1); mbar_init(bar(B_QFULLP + s), 1); mbar_init(bar(B_QEMPTY + s), 1);
-            mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_SFREE + s), 8);
-            mbar_init(bar(B_PFULL + s), 8); mbar_init(bar(B_PFREE + s), 1);
-            mbar_init(bar(B_MRFULL + s), 128); mbar_init(bar(B_MREMPTY + s), 128);
-            mbar_init(bar(B_LSFULL + s), 256); mbar_init(bar(B_LSEMPTY + s), 128);
-        }
-        for (int s = 0; s < 4; ++s) {
-            mbar_init(bar(B_KFULL + s), 1); mbar_init(bar(B_KFULLP + s), 1); mbar_init(bar(B_KEMPTY + s), 1);
-            mbar_init(bar(B_VFULL + s), 1); mbar_init(bar(B_VFULLP + s), 1); mbar_init(bar(B_VEMPTY + s), 1);
-        }
-        mbar_init(bar(B_OFULL), 1);
-        mbar_init(bar(B_OFREE), 8);
-        mbar_init(bar(B_EPIDONE), 128);
-        *abort_flag = 0;
+    // this pair's records: the offsets are requested first, the barriers are set up while they travel
+    const int rec0 = a_param.sched_off[pair];
+    const int n_rounds = a_param.sched_off[pair + 1] - rec0;
+    if (tid < B_COUNT) {
+        // one barrier per thread; arrival counts: 8 = one elected lane per warp of a warpgroup in both CTAs, 128 / 256 =
+        // every thread of one / two warpgroups of this CTA, 1 = one thread, a tcgen05.commit or a loader's lane 0
+        const int b = tid;
+        int count = 1;
+        if (b == B_SFREE || b == B_SFREE + 1 || b == B_PFULL || b == B_PFULL + 1 || b == B_OFREE) count = 8;
+        else if (b == B_LSFULL || b == B_LSFULL + 1) count = 256;
+        else if (b >= B_MRFULL) count = 128;   // MRFULL, MREMPTY, LSEMPTY, EPIDONE
+        mbar_init(bar(b), count);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    if (tid == 0) *abort_flag = 0;
     if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
@@ -208,9 +205,6 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
     // This CTA's barriers and TMEM are ready: tell the peer now, and wait for the peer (cluster_wait, inside the roles)
     // only where something first crosses the pair.  Loads into this CTA's own shared memory start before that.
     cluster_arrive();
-    // this pair's records
-    const int rec0 = a_param.sched_off[pair];
-    const int n_rounds = a_param.sched_off[pair + 1] - rec0;
     const SchedRec* recs_g = a_param.sched_recs + rec0;
     SchedRec* recs_s = reinterpret_cast<SchedRec*>(gbase + OFF_ITEMS);
     {
@@ -292,29 +286,30 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                 }
                 if (warp_valid) {
                     const int key0 = (it.t0 + tile_of(jj, n)) * TILE_N;
-                    float mx_any = -INFINITY;
-                    if (key0 + TILE_N > it.full_until) {
-                        // the tile touches a mask boundary: write -inf over the hidden scores in TMEM first
-#pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t wv[32];
-                            tmem_ld32(tS + c * 32, wv);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                if (jj == 0 && key0 + c * 32 + e < it.total) mx_any = fmaxf(mx_any, __uint_as_float(wv[e]));
-                                if (key0 + c * 32 + e >= limit) wv[e] = 0xff800000u;
-                            }
-                            tmem_st32(tS + c * 32, wv);
-                        }
-                        tmem_st_wait();
-                    }
                     uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(bar0(B_SFREE + w));   // the next Q K^T into this buffer may start
+                    float mx_any = -INFINITY;
+                    if (key0 + TILE_N > it.full_until) {
+                        // The tile touches a mask boundary (warp-uniform; one or two tiles per item): hidden scores become
+                        // -inf in registers.  Only an item's first tile needs the maximum over its hidden keys as well.
+                        const int rel = limit - key0, rel_any = it.total - key0;
+                        if (jj == 0) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                                for (int e = 0; e < 32; ++e)
+                                    if (c * 32 + e < rel_any) mx_any = fmaxf(mx_any, __uint_as_float(v[c][e]));
+                        }
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                if (c * 32 + e >= rel) v[c][e] = 0xff800000u;
+                    }
                     if (jj == 0) {
                         // First tile of the item: its row maximum becomes the fixed reference of the row.
                         float mx4[4];
@@ -337,30 +332,37 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                         m_ref = xm[slot * 128 + L];
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    // P = exp2(s * scale - m_ref) as bf16, a whole row in registers first: the exponentials do not need the
-                    // P buffer, only the stores at the end do, and by then the P V that last read the buffer has long run
+                    // P = exp2(s * scale - m_ref) as bf16.  The first half of the row is kept in registers: the exponentials
+                    // do not need the P buffer, only the stores do, and half a row later the P V that last read the
+                    // buffer has run (waiting for it up front would stall here, a whole row in registers costs too many)
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
-                    uint32_t pk[4][16];
+                    uint32_t pk[2][16];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
+                        uint32_t pc[16];
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            if (c < 2) pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y); else pc[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                        }
+                        if (c == 1) {
+                            if (u >= 1) {
+                                // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
+                                // this buffer must have been consumed before the next one goes in
+                                bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
+                                if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
+                                tc_fence_after();
+                            }
+                            tmem_st16(tP, pk[0]);
+                            tmem_st16(tP + 16, pk[1]);
+                        } else if (c >= 2) {
+                            tmem_st16(tP + c * 16, pc);
                         }
                     }
-                    if (u >= 1) {
-                        // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in this
-                        // buffer must have been consumed before the next one goes in
-                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                        tc_fence_after();
-                    }
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tmem_st16(tP + c * 16, pk[c]);
+                    if (!alive) break;
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     const float tsum = lacc0.x + lacc0.y;
                     out_of_range |= !(tsum <= DLX_SUM_HIGH);   // also catches NaN
@@ -727,10 +729,7 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     const int idx = ck + k;
                     ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
                     if (!ok) break;
-                    // rows written by cp.async (a tile with the end of the prefix) must be visible to the tensor cores,
-                    // which read this CTA's half from this CTA's shared memory: proxy fence here, then the signal
-                    if ((it.t0 + tile_of(k, n)) * TILE_N + K_ROWS * rank + K_ROWS > it.ctx) fence_async_proxy();
-                    mbar_arrive_cluster(bar0(B_KFULLP + idx % KSTAGES));
+                    mbar_arrive_cluster(bar0(B_KFULLP + idx % KSTAGES));   // (TMA wrote the half: no proxy fence needed)
                     if (k == 0) prefetch_upto(done + 2);   // the next item's Q, into the other buffer
                 }
             } else {
@@ -750,8 +749,7 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     ok = mbar_wait(bar(B_KFULL + st), par, abort_flag, 10, k);
                     ok = ok && mbar_wait_cluster(bar(B_KFULLP + st), par, abort_flag, 13, k);
                     if (!ok) break;
-                    fence_async_proxy();
-                    tc_fence_after();
+                    tc_fence_after();   // K, V and Q were written by TMA copies: the async proxy already sees them
                     const uint32_t kb = sK + st * K_STAGE;
                     const uint32_t d = tmem + TM_S + b * 128;
                     const uint64_t dq = smem_desc(qaddr, 16, 1024), dk = smem_desc(kb, 16, 1024);
@@ -787,7 +785,6 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     const int idx = ck + k;
                     ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k);
                     if (!ok) break;
-                    if ((it.t0 + tile_of(k, n)) * TILE_N + TILE_N > it.ctx) fence_async_proxy();
                     mbar_arrive_cluster(bar0(B_VFULLP + idx % VSTAGES));
                 }
             } else {
@@ -802,8 +799,7 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     ok = ok && mbar_wait_cluster(bar(B_VFULLP + st), par, abort_flag, 14, k);
                     ok = ok && mbar_wait_cluster(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                     if (!ok) break;
-                    fence_async_proxy();
-                    tc_fence_after();
+                    tc_fence_after();   // K, V and Q were written by TMA copies: the async proxy already sees them
                     const uint32_t vb = sV + st * V_STAGE;
                     const uint32_t pa = tmem + TM_P + b * 64;
                     const uint64_t dv = smem_desc(vb, V_STAGE, 1024);

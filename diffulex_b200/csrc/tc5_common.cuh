@@ -135,6 +135,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
 }
 
+
 // ---- cluster (CTA pair) forms ----------------------------------------------------------------------------------
 // Address of the same shared-memory offset in CTA `rank` of the cluster (a shared::cluster address).
 __device__ __forceinline__ uint32_t map_to_cta(uint32_t addr, uint32_t rank) {
