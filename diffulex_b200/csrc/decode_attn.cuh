@@ -39,6 +39,7 @@ struct DecodeArgs {
     int64_t page_stride, token_stride;  // cache strides, elements
     int64_t bt_stride, num_pages;
     int total_q, num_seqs, max_blocks, max_q_len;
+    int total_kv;   // rows of k / v
     int hq, hkv, group, page_size;
     int mask_mode, dbs;
     int num_splits, m_blocks;
@@ -48,7 +49,8 @@ struct DecodeArgs {
     int q_by_tma;      // tcgen05 kernel: Q blocks are fetched by TMA (else by 16-byte cp.async)
     int items_total;   // tcgen05 kernels: num_seqs * hkv * m_blocks * num_splits work items, walked by persistent CTAs
     int bins;          // tcgen05 kernels: persistent CTAs (single-CTA kernel) or CTA pairs (pair kernel) of the launch
-    int tokens_per_item;  // tcgen05 kernels: query tokens of one work item (pair kernel: two blocks of q_tokens)
+    int tokens_per_item;  // tcgen05 kernels: query tokens of one work item (two blocks of q_tokens when two CTAs share an item)
+    int group_ctas;       // tcgen05 kernels: CTAs that work on the same schedule bin (1, or 2: each takes one block of q_tokens)
     float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -68,8 +70,10 @@ int launch_combine(const DecodeArgs& a, int head_dim, cudaStream_t st);
 bool tc5_eligible(int group, int head_dim);
 int launch_decode_tc5(const DecodeArgs& a, cudaStream_t st);
 int launch_decode_tc5_pair(const DecodeArgs& a, cudaStream_t st);
-// Fills a.bins / a.tokens_per_item / a.m_blocks / a.items_total for the chosen tcgen05 kernel.
-void tc5_plan_items(DecodeArgs& a, bool pair, int sm_count);
+// Fills a.bins / a.tokens_per_item / a.group_ctas / a.m_blocks / a.items_total for the chosen tcgen05 kernel.  `two_ctas`:
+// an item is 2 x (128 / group) query tokens taken by two CTAs (the CTA-pair kernel, or two neighbouring CTAs of the
+// single-CTA kernel that walk the same record list, so that the second reader of a K / V tile finds it in L2).
+void tc5_plan_items(DecodeArgs& a, bool two_ctas, int sm_count);
 // Builds the schedule of a launch (a.sched_off / a.sched_recs must point into a buffer of sched_bytes(a.items_total)).
 int launch_decode_sched(const DecodeArgs& a, cudaStream_t st);
 int device_sm_count();

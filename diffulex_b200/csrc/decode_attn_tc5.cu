@@ -56,21 +56,19 @@ constexpr int KSTAGES = DLX_KSTAGES, VSTAGES = DLX_VSTAGES;
 constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_V = OFF_K + KSTAGES * ITEM_BYTES;
 constexpr int OFF_BAR = OFF_V + VSTAGES * ITEM_BYTES;
-constexpr int OFF_TAB = OFF_BAR + 512;             // row-source pointer tables: one per loader warp, 128 rows
-constexpr int OFF_BT = OFF_TAB + 2 * TILE_N * 8;   // this sequence's page ids, one copy per loader warp
-constexpr int BT_SLOTS = 512;                      // 2 KiB per loader warp: 131 k tokens at 256-token pages
+constexpr int OFF_BT = OFF_BAR + 512;              // page ids of a long item that its record does not hold, one copy per loader warp
+constexpr int BT_SLOTS = 512;                      // 2 KiB per loader warp
 constexpr int OFF_XCH = OFF_BT + 2 * BT_SLOTS * 4; // 8 x 128 floats: two slots of row references; two slots of (row sums x 2, reference)
 constexpr int OFF_STAGE = OFF_XCH + 8 * 128 * 4;   // output staging: 32 rows x 128 bytes per epilogue warp
 constexpr int STAGE_WARP_BYTES = 32 * 128;
 constexpr int OFF_ROWMAP = OFF_STAGE + 4 * STAGE_WARP_BYTES;   // int2[128]: (row / group, row % group) of a block's rows
-constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;   // this CTA's decoded work items, one per round
-constexpr int MAX_ROUNDS = 64;                     // more rounds than this: every role decodes its items itself
-constexpr int ITEM_SLOT = 64;                      // bytes per decoded item
-constexpr int OFF_FLAGS = OFF_ITEMS + MAX_ROUNDS * ITEM_SLOT;  // one bit per round: the item has to be computed again, exactly
+constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;   // this CTA's schedule records, one per round
+constexpr int MAX_ROUNDS = 48;                     // records kept in shared memory; later rounds are read from global
+constexpr int OFF_FLAGS = OFF_ITEMS + MAX_ROUNDS * (int)sizeof(SchedRec);  // one bit per round: the item has to be computed again, exactly
 constexpr int FLAG_WORDS = 128;                    // 4096 rounds; later rounds share the bits
 constexpr int OFF_ARGS = OFF_FLAGS + FLAG_WORDS * 4;   // a copy of the argument block (256 bytes)
-constexpr int SMEM_BYTES = OFF_ARGS + 256 + 1024;  // + slack for 1024-byte alignment
-static_assert(sizeof(DecodeArgs) <= 256, "argument block copy");
+constexpr int SMEM_BYTES = OFF_ARGS + 320 + 1024;  // + slack for 1024-byte alignment
+static_assert(sizeof(DecodeArgs) <= 320, "argument block copy");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 // P = 2^(s*scale*log2e - m_ref) with m_ref fixed by the first tile.  Floating point keeps full relative
 // precision however far later scores lie from m_ref, until 2^x leaves the bf16/fp32 range: an item in which a tile's
@@ -88,7 +86,6 @@ constexpr int SOFTMAX_REGS = DLX_SOFTMAX_REGS, HELPER_REGS = DLX_HELPER_REGS, EP
 static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget");
 constexpr int EPI_WARP0 = 12;
 constexpr int KLOAD_WARP = 8, VLOAD_WARP = 9, QK_WARP = 10, PV_WARP = 11;
-constexpr int NUM_LOADERS = 32;                    // lanes of one loader warp
 // TMEM columns (512): two S buffers of 128 fp32 columns, two P buffers of 64 columns (128 bf16 keys), O
 constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
 
@@ -125,9 +122,10 @@ struct alignas(8) Item {
     int row0, rows_here, tok0;   // first packed row (= tok0 * group), valid rows, first token of the block
     int cta_limit, full_until;
     int t0, n;
+    int first_page, n_pages;     // the record holds the ids of pages [first_page, first_page + n_pages)
 };
 
-__device__ __forceinline__ Item load_item(const DecodeArgs& a, const SchedRec* r) {
+__device__ __forceinline__ Item load_item(const DecodeArgs& a, const SchedRec* r, int rank) {
     Item it;
     const int4 w0 = *reinterpret_cast<const int4*>(&r->seq);
     const int4 w1 = *reinterpret_cast<const int4*>(&r->q0);
@@ -138,11 +136,15 @@ __device__ __forceinline__ Item load_item(const DecodeArgs& a, const SchedRec* r
     it.valid = (w2.w & SCHED_VALID) != 0;
     it.empty_split = (w2.w & SCHED_EMPTY_SPLIT) != 0;
     it.total = it.ctx + it.nnew;
+    it.first_page = r->first_page; it.n_pages = r->n_pages;
     // A block holds q_tokens = 128 / group whole tokens (all `group` heads of each), so that its Q rows are one box
     // of the [token][head][head_dim] tensor; packed row r of the (sequence, KV head) is token r / group, head r % group.
-    it.tok0 = w0.z * a.q_tokens;
+    // With two CTAs per schedule bin an item is two such blocks and CTA `rank` of the bin takes the rank-th one; a
+    // CTA whose block lies past the end of a short sequence has nothing to do for the item.
+    it.tok0 = w0.z * a.tokens_per_item + rank * a.q_tokens;
     it.row0 = it.tok0 * a.group;
     it.rows_here = max(min(w1.y - it.tok0, a.q_tokens), 0) * a.group;
+    if (it.rows_here == 0) { it.valid = false; it.empty_split = false; }
     it.cta_limit = r->limit;
     it.full_until = it.total;
     if (a.mask_mode == DLX_MASK_BLOCK_CAUSAL) it.full_until = it.ctx + min(it.nnew, (it.tok0 / a.dbs + 1) * a.dbs);
@@ -156,10 +158,14 @@ __device__ __forceinline__ Item load_item(const DecodeArgs& a, const SchedRec* r
 // warpgroup waits for: a full tile delivers them sooner, while the other warpgroup masks the last tile.
 __device__ __forceinline__ int tile_of(int jj, int n) { return n - 1 - ((jj < 2 && n >= 2) ? (jj ^ 1) : jj); }
 
-// Tensor maps of one launch: the K and V caches as {head_dim, Hkv, page row, page} with boxes of 128 >> level rows
-// (level 0..4: 128, 64, 32, 16, 8 rows; levels whose box would exceed a page are unused), and Q.
+// Tensor maps of one launch, by level l = 0..7: boxes of 128 >> l rows x 64 head_dim columns.  kc / vc: the caches as
+// {head_dim, Hkv, page row, page}; kn / vn: the in-flight rows as {head_dim, Hkv, token}.  Levels whose box exceeds a
+// page (caches) are unused.  Any run of rows is a few boxes of falling size; a box may start at any row of a tile:
+// the 128-byte swizzle of a copy follows the shared-memory address it writes.
+constexpr int LEVELS = 8;
 struct TmaMaps {
-    CUtensorMap k[5], v[5], q;
+    CUtensorMap kc[LEVELS], vc[LEVELS], kn[LEVELS], vn[LEVELS];
+    CUtensorMap q;
 };
 
 // Persistent kernel: one CTA per SM walks its rounds of the (longest-first) item list.  Every role keeps running
@@ -190,10 +196,10 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     const int G = a_param.group;
 
     if (tid == 0) {
-        mbar_init(bar(B_QFULL), a_param.q_by_tma ? 1 : NUM_LOADERS);
+        mbar_init(bar(B_QFULL), 1);
         mbar_init(bar(B_QEMPTY), 1);
-        for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), NUM_LOADERS); mbar_init(bar(B_KEMPTY + s), 1); }
-        for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), NUM_LOADERS); mbar_init(bar(B_VEMPTY + s), 1); }
+        for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), 1); mbar_init(bar(B_KEMPTY + s), 1); }
+        for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), 1); mbar_init(bar(B_VEMPTY + s), 1); }
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128);
             mbar_init(bar(B_SFREE + s), 128); mbar_init(bar(B_PFREE + s), 1);
@@ -209,18 +215,27 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     // This CTA's records: placed by the schedule kernel (longest-processing-time greedy, longest item first).
-    const int rec0 = a_param.sched_off[blockIdx.x];
-    const int n_rounds = a_param.sched_off[blockIdx.x + 1] - rec0;
+    // (two neighbouring CTAs walk the same list when an item is two row blocks: they run side by side, and the second
+    // reader of a K / V tile finds it in L2)
+    const int bin = (int)blockIdx.x / a_param.group_ctas, rank = (int)blockIdx.x - bin * a_param.group_ctas;
+    const int rec0 = a_param.sched_off[bin];
+    const int n_rounds = a_param.sched_off[bin + 1] - rec0;
     const SchedRec* recs_g = a_param.sched_recs + rec0;
-    Item* items_s = reinterpret_cast<Item*>(gbase + OFF_ITEMS);   // ITEM_SLOT >= sizeof(Item); indexed as Item[]
-    if (tid < min(n_rounds, MAX_ROUNDS)) items_s[tid] = load_item(a_param, recs_g + tid);
+    SchedRec* recs_s = reinterpret_cast<SchedRec*>(gbase + OFF_ITEMS);
+    {
+        const int n_tab = min(n_rounds, MAX_ROUNDS);
+        const uint4* src = reinterpret_cast<const uint4*>(recs_g);
+        uint4* dst = reinterpret_cast<uint4*>(recs_s);
+        for (int i = tid; i < n_tab * (int)(sizeof(SchedRec) / 16); i += NUM_THREADS) dst[i] = src[i];
+    }
+    auto rec_of = [&](int k) -> const SchedRec* { return k < MAX_ROUNDS ? recs_s + k : recs_g + k; };
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
     int2* rowmap = reinterpret_cast<int2*>(gbase + OFF_ROWMAP);
     if (tid >= 128 && tid < 256) rowmap[tid - 128] = make_int2((tid - 128) / G, (tid - 128) % G);
     uint32_t* redo_flags = reinterpret_cast<uint32_t*>(gbase + OFF_FLAGS);
     if (tid >= 256 && tid < 256 + FLAG_WORDS) redo_flags[tid - 256] = 0;
-    auto get_item = [&](int k) { return k < MAX_ROUNDS ? items_s[k] : load_item(a, recs_g + k); };
+    auto get_item = [&](int k) { return load_item(a, rec_of(k), rank); };
     {
         // Q rows past the last whole token of a block (e.g. rows 126, 127 for 7 heads per KV head) are never written
         // by a Q box: zero them once, so that the unused TMEM lanes only ever see finite scores.
@@ -231,26 +246,9 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         }
         // The K and V rings start out as zeros: rows that no copy writes (past the last key of a tail tile) must hold
         // finite values, because 0 x NaN would poison the P V product.
-        if (a_param.tma_box_rows > 0)
-            for (int i = tid; i < (KSTAGES + VSTAGES) * ITEM_BYTES / 16; i += NUM_THREADS)
-                *reinterpret_cast<uint4*>(gbase + OFF_K + i * 16) = make_uint4(0, 0, 0, 0);
+        for (int i = tid; i < (KSTAGES + VSTAGES) * ITEM_BYTES / 16; i += NUM_THREADS)
+            *reinterpret_cast<uint4*>(gbase + OFF_K + i * 16) = make_uint4(0, 0, 0, 0);
         fence_async_proxy();
-    }
-    // The loader warps fetch the page ids of the CTA's first item already now, next to the table fill above (their
-    // own decode of the item): otherwise this third dependent load would start only after the set-up barrier.
-    bool bt_preloaded = false;
-    if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
-        Item f; f.valid = false;
-        if (n_rounds > 0) f = load_item(a_param, recs_g);
-        if (f.valid) {
-            const int pages = min((f.ctx + a_param.page_size - 1) / a_param.page_size, a_param.max_blocks);
-            if (pages <= BT_SLOTS) {
-                const int32_t* bt_g = a_param.block_tables + (int64_t)f.seq * a_param.bt_stride;
-                int32_t* bt_s = reinterpret_cast<int32_t*>(gbase + OFF_BT) + (warp == VLOAD_WARP ? BT_SLOTS : 0);
-                for (int j = lane; j < pages; j += 32) bt_s[j] = bt_g[j];
-                bt_preloaded = true;
-            }
-        }
     }
     if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
@@ -573,159 +571,123 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     } else {
     reg_dec<HELPER_REGS>();   // one site for the whole helper warpgroup (warps 8..11)
     if (warp == KLOAD_WARP || warp == VLOAD_WARP) {
-        // =========================== loaders: one warp for K tiles, one for V tiles (and later items' Q) ==========
+        // =========================== loaders: one warp for K tiles, one for V tiles ===========================
         // Separate warps so that K (needed two tiles ahead by Q K^T) never queues behind a V tile that is still
-        // waiting for its ring slot.  The rings run across items: while the softmax works on the tail of one item,
-        // the first tiles of the next are already landing.
+        // waiting for its ring slot.  The rings run across items.  Every tile comes by TMA, issued by lane 0: the
+        // common tile (inside the cached prefix, one box per head_dim half) on a short path with ring position and
+        // page tracked incrementally and the page id taken from the record; the tile with the end of the prefix and
+        // the in-flight rows as a few boxes of falling size (128 >> level rows), cached rows from the cache maps,
+        // in-flight rows from the maps over k / v.
         const int which = warp == VLOAD_WARP;          // 0: K, 1: V
-        const int col = lane & 15, rbase = lane >> 4;  // 16-byte chunk of the row; rows rbase + 2 i
-        const uint32_t half_off = (col >> 3) * REGION;
-        const int c8 = col & 7;
-        const char* qp = static_cast<const char*>(a.q);
-        const char* cache = static_cast<const char*>(which ? a.v_cache : a.k_cache);
-        const char* fresh = static_cast<const char*>(which ? a.v : a.k);
-        const int64_t fresh_rs = which ? a.v_rs : a.k_rs;
         int32_t* bt_base = reinterpret_cast<int32_t*>(gbase + OFF_BT) + which * BT_SLOTS;
-        // Row-source table for tiles that go through cp.async: where each key row's bytes start (nullptr = row past
-        // the end, zero-filled).  Four rows per lane; one table per loader warp, rebuilt per tile.
-        const char** tab = reinterpret_cast<const char**>(gbase + OFF_TAB) + which * TILE_N;
         const int stages = which ? VSTAGES : KSTAGES;
+        const int box_rows0 = a.tma_box_rows, lvl0 = a.tma_lvl0;   // largest cache box: min(128, page size) rows
+        const CUtensorMap* cmaps = which ? maps.vc : maps.kc;
+        const CUtensorMap* nmaps = which ? maps.vn : maps.kn;
+        const int page_size = a.page_size;
+        const bool one_box_geom = box_rows0 == TILE_N && page_size % TILE_N == 0;   // a whole tile is one box per half
+        const int tiles_per_page = page_size / TILE_N;         // used only with one_box_geom
+        const uint32_t bar_full0 = bar(which ? B_VFULL : B_KFULL), bar_empty0 = bar(which ? B_VEMPTY : B_KEMPTY);
+        const uint32_t ring0 = which ? sV : sK;
+        int stage = 0;            // ring position of the next tile
+        uint32_t par_empty = 1;   // parity of "this slot is free" for the next tile (the first pass finds every slot free)
         bool alive = true;
 #pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
-            const Item it = get_item(round);
+            const SchedRec* rec = rec_of(round);
+            const Item it = load_item(a, rec, rank);
             if (!it.valid) continue;
             const int n = it.n, ctx = it.ctx, kvh = it.kvh;
             const int32_t* bt_g = a.block_tables + (int64_t)it.seq * a.bt_stride;
-            // This sequence's page ids go to shared memory once per item (a per-tile global lookup would put an L2 round
-            // trip in front of every tile's copies); each loader warp keeps its own copy.  Longer tables stay global.
-            const int pages_needed = min((ctx + a.page_size - 1) / a.page_size, a.max_blocks);
-            const bool bt_in_smem = pages_needed <= BT_SLOTS;
+            // Page ids: the record holds the last n_pages of the range; a longer item's earlier ids are copied to shared
+            // memory in the background (4-byte cp.async) and first read many tiles later.
+            const int early = min(it.first_page, BT_SLOTS);
+            bool early_ready = early == 0;
             __syncwarp();
-            if (bt_in_smem && !(round == 0 && bt_preloaded))
-                for (int j = lane; j < pages_needed; j += 32) bt_base[j] = bt_g[j];
-            const int32_t* bt = bt_in_smem ? bt_base : bt_g;
-            __syncwarp();
-            if (which == 1 && !a.q_by_tma) {
-                // Q without TMA (the Q K^T issuer fetches it otherwise): 16-byte cp.async as soon as the last Q K^T of
-                // the previous item has run; rows past the item's end are zero-filled.
-                if (done > 0) {
-                    bool okq = mbar_wait(bar(B_QEMPTY), (done - 1) & 1, abort_flag, 6, -2);
-                    if (!__all_sync(0xffffffffu, okq)) { alive = false; break; }
-                }
-                const int head0 = kvh * G;
-                int qi = (it.row0 + rbase) / G, qg = (it.row0 + rbase) % G;
-#pragma unroll 1
-                for (int i = 0; i < 64; ++i) {
-                    const int row = rbase + 2 * i;
-                    const bool okr = row < it.rows_here;
-                    const char* src = qp + (((int64_t)(it.q0 + qi) * a.q_rs + (int64_t)(head0 + qg) * HD + col * 8) << 1);
-                    cp_async_16(sQ + half_off + row * 128 + ((c8 ^ (row & 7)) << 4), okr ? src : qp, okr ? 16 : 0);
-                    qg += 2;
-                    while (qg >= G) { qg -= G; ++qi; }
-                }
-                cp_async_arrive(bar(B_QFULL));
-            }
+            for (int j = lane; j < early; j += 32)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(bt_base + j)), "l"(bt_g + j) : "memory");
+            const int first_page = it.first_page, n_pages = it.n_pages;
+            auto page_id = [&](int j) -> int {
+                if ((unsigned)(j - first_page) < (unsigned)n_pages) return rec->pages[j - first_page];
+                if (j >= a.max_blocks) return -1;
+                if (j < early) return bt_base[j];
+                return bt_g[j];
+            };
+            // (page, tile inside the page) of the item's last tile; the walk goes n-2, n-1, n-3, n-4, ..., 0
+            int pj_hi = 0, sub_hi = 0;
+            if (one_box_geom) { pj_hi = (it.t0 + n - 1) / tiles_per_page; sub_hi = (it.t0 + n - 1) - pj_hi * tiles_per_page; }
+            int pj_w = pj_hi, sub_w = sub_hi;     // walking position
 #pragma unroll 1
             for (int jj = 0; jj < n && alive; ++jj) {
-                const int idx = ck + jj;                       // running tile count: ring position
-                const int stage = idx % stages;
-                const uint32_t par_empty = ((idx / stages) & 1) ^ 1;
-                const int p0 = (it.t0 + tile_of(jj, n)) * TILE_N;
-                const bool tma_on = a.tma_box_rows > 0;
-                const bool by_tma = tma_on && p0 + TILE_N <= ctx;
-                // A tile that holds the end of the cached prefix: its leading cached rows, in whole groups of 8 (the
-                // swizzle period), still come by TMA, as boxes of 64, 32, 16 and 8 rows; rows [tma_rows, c_end) go
-                // through cp.async.  With TMA on, rows past the last key are not written at all: they keep what an
-                // earlier tile (or the zero fill at kernel start) left there, which is finite, and their scores are
-                // masked to -inf.
-                int tma_rows = 0, c_end = TILE_N;
-                if (!by_tma && tma_on) {
-                    tma_rows = max(min(ctx - p0, TILE_N), 0) & ~7;
-                    c_end = min(it.total - p0, TILE_N);
+                const int tl = tile_of(jj, n);
+                int pj = pj_hi, sub = sub_hi;
+                if (jj != 1 && n >= 2) {
+                    if (--sub_w < 0) { sub_w = tiles_per_page - 1; --pj_w; }
+                    pj = pj_w; sub = sub_w;
                 }
-                // With TMA on, pages are walked incrementally from the tile's first (page, row): one division per tile.
-                int pj = 0, prow = 0;
-                if (tma_on) { pj = p0 / a.page_size; prow = p0 - pj * a.page_size; }
-                if (!by_tma) {
-                    int pj2 = pj, prow2 = prow + tma_rows;   // page and row of key p0 + tma_rows
-                    if (tma_on && prow2 >= a.page_size) { pj2 += prow2 / a.page_size; prow2 %= a.page_size; }
-                    const int64_t pid2 = (tma_on && pj2 < a.max_blocks) ? (int64_t)bt[pj2] : -1;
-#pragma unroll 1
-                    for (int hh = 0; hh < 4; ++hh) {
-                        const int row = tma_rows + lane + 32 * hh;
-                        if (row >= c_end) break;
-                        const int p = p0 + row;
-                        const char* ptr = nullptr;
-                        if (p < ctx) {
-                            if (tma_on) {   // the cached rows left over after the boxes: fewer than 8, all in one page
-                                if (pid2 >= 0 && pid2 < a.num_pages)
-                                    ptr = cache + ((pid2 * a.page_stride + (int64_t)(prow2 + row - tma_rows) * a.token_stride + kvh * HD) << 1);
-                            } else {
-                                const int j = p / a.page_size;
-                                const int64_t pid = j < a.max_blocks ? (int64_t)bt[j] : -1;
-                                if (pid >= 0 && pid < a.num_pages)
-                                    ptr = cache + ((pid * a.page_stride + (int64_t)(p - j * a.page_size) * a.token_stride + kvh * HD) << 1);
-                            }
-                        } else if (p < it.total) {
-                            ptr = fresh + (((int64_t)(it.kv0 + (p - ctx)) * fresh_rs + kvh * HD) << 1);
+                const int p0 = (it.t0 + tl) * TILE_N;   // first key of the tile
+                const uint32_t full = bar_full0 + 8u * stage;
+                const uint32_t d0 = ring0 + stage * ITEM_BYTES;
+                bool ok = true;
+                if (lane == 0) {
+                    if (one_box_geom && p0 + TILE_N <= ctx) {
+                        // ---- the common tile ----
+                        if (!early_ready && pj < early) {
+                            asm volatile("cp.async.wait_all;\n" ::: "memory");
+                            early_ready = true;
                         }
-                        tab[row] = ptr;
-                    }
-                    __syncwarp();
-                }
-                // Everything a whole-tile copy needs is worked out BEFORE the wait for the ring slot: what follows the wait
-                // is on the critical path of a two- or three-deep ring (slot freed -> copy issued -> data -> MMA).
-                const uint32_t full = bar((which ? B_VFULL : B_KFULL) + stage);
-                const uint32_t d0 = (which ? sV : sK) + stage * ITEM_BYTES;
-                const CUtensorMap* lvl_maps = which ? maps.v : maps.k;
-                const bool one_box = by_tma && a.tma_box_rows == TILE_N;   // the tile is one box (pair) of one page
-                const int pid0 = (one_box && pj < a.max_blocks) ? bt[pj] : -1;   // a bad id is out of bounds: zero fill
-                bool ok = mbar_wait(bar((which ? B_VEMPTY : B_KEMPTY) + stage), par_empty, abort_flag, 5 + which, jj);
-                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                if (one_box) {
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(full, ITEM_BYTES);
-                        tma_load_4d(d0, &lvl_maps[0], 0, kvh, prow, pid0, full);
-                        tma_load_4d(d0 + REGION, &lvl_maps[0], 64, kvh, prow, pid0, full);
+                        const int pid0 = page_id(pj);
+                        const int prow = sub * TILE_N;
+                        ok = mbar_wait(bar_empty0 + 8u * stage, par_empty, abort_flag, 5 + which, jj);
+                        if (ok) {
+                            mbar_arrive_expect_tx(full, ITEM_BYTES);
+                            tma_load_4d(d0, &cmaps[lvl0], 0, kvh, prow, pid0, full);
+                            tma_load_4d(d0 + REGION, &cmaps[lvl0], 64, kvh, prow, pid0, full);
+                        }
                     } else {
-                        mbar_arrive(full);
-                    }
-                } else if (by_tma || tma_rows > 0) {
-                    if (lane == 0) {
-                        const int rows_by_tma = by_tma ? TILE_N : tma_rows;
-                        if (by_tma) mbar_arrive_expect_tx(full, ITEM_BYTES);
-                        else mbar_expect_tx(full, (uint32_t)tma_rows * 256u);
-                        int r0 = 0;
-                        int lvl = a.tma_lvl0;                        // largest usable box: min(128, page_size) rows
+                        // ---- the tile with the end of the prefix, in-flight rows, small pages ----
+                        const int cr = max(min(ctx - p0, TILE_N), 0);        // cached rows of the tile
+                        const int ce = max(min(it.total - p0, TILE_N), 0);   // ... plus in-flight rows; the rest stays as it is
+                        int pjg = p0 / page_size, prow = p0 - pjg * page_size;
+                        if (!early_ready && pjg < early && cr > 0) {
+                            asm volatile("cp.async.wait_all;\n" ::: "memory");
+                            early_ready = true;
+                        }
+                        ok = mbar_wait(bar_empty0 + 8u * stage, par_empty, abort_flag, 5 + which, jj);
+                        if (ok) {
+                            if (ce == 0) {
+                                mbar_arrive(full);
+                            } else {
+                                mbar_arrive_expect_tx(full, (uint32_t)ce * 256u);
+                                int r = 0;
+                                int lvl = lvl0;
 #pragma unroll 1
-                        for (int sz = TILE_N >> lvl; sz >= 8; sz >>= 1, ++lvl) {
-                            while (rows_by_tma - r0 >= sz) {         // more than once only at the largest size
-                                const int pid = pj < a.max_blocks ? bt[pj] : -1;   // a bad id is out of bounds: zero fill
-                                tma_load_4d(d0 + r0 * 128, &lvl_maps[lvl], 0, kvh, prow, pid, full);
-                                tma_load_4d(d0 + REGION + r0 * 128, &lvl_maps[lvl], 64, kvh, prow, pid, full);
-                                r0 += sz; prow += sz;
-                                if (prow >= a.page_size) { prow = 0; ++pj; }   // boxes never straddle a page
+                                for (int sz = box_rows0; sz >= 1; sz >>= 1, ++lvl) {
+                                    while (cr - r >= sz) {
+                                        const int pid = page_id(pjg);   // a bad id is out of bounds: zero fill
+                                        tma_load_4d(d0 + r * 128, &cmaps[lvl], 0, kvh, prow, pid, full);
+                                        tma_load_4d(d0 + REGION + r * 128, &cmaps[lvl], 64, kvh, prow, pid, full);
+                                        r += sz; prow += sz;
+                                        if (prow >= page_size) { prow = 0; ++pjg; }   // boxes never straddle a page
+                                    }
+                                }
+                                int tok = it.kv0 + (p0 + cr - ctx);   // first in-flight row of the tile
+                                lvl = 0;
+#pragma unroll 1
+                                for (int sz = TILE_N; sz >= 1; sz >>= 1, ++lvl) {
+                                    while (ce - r >= sz) {
+                                        tma_load_3d(d0 + r * 128, &nmaps[lvl], 0, kvh, tok, full);
+                                        tma_load_3d(d0 + REGION + r * 128, &nmaps[lvl], 64, kvh, tok, full);
+                                        r += sz; tok += sz;
+                                    }
+                                }
                             }
                         }
-                    } else if (by_tma) {
-                        mbar_arrive(full);
                     }
                 }
-                if (!by_tma) {
-                    const uint32_t dbase = d0 + half_off;
-                    const int pairs = (c_end - tma_rows + 1) >> 1;
-#pragma unroll 2
-                    for (int i = 0; i < pairs; ++i) {
-                        const int row = tma_rows + rbase + 2 * i;
-                        if (row < c_end) {
-                            const char* rp = tab[row];
-                            cp_async_16(dbase + row * 128 + ((c8 ^ (row & 7)) << 4), rp ? rp + col * 16 : qp, rp ? 16 : 0);
-                        }
-                    }
-                    cp_async_arrive(full);
-                    __syncwarp();  // the table is rebuilt for the next tile
-                }
+                early_ready = __shfl_sync(0xffffffffu, (int)early_ready, 0) != 0;
+                alive = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+                if (++stage == stages) { stage = 0; par_empty ^= 1u; }
             }
             ++done; ck += n;
         }
@@ -743,7 +705,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             const Item it = get_item(round);
             if (!it.valid) continue;
             const int n = it.n;
-            if (a.q_by_tma) {
+            {
                 // Q of this item: one box per head_dim half, as soon as the last Q K^T of the previous item has run
                 // (this thread's own commit).  Tokens past the end of the tensor read as zero; tokens of the next
                 // sequence are loaded but their rows are never stored.
@@ -764,7 +726,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 }
                 ok = mbar_wait(bar(B_KFULL + idx % KSTAGES), (idx / KSTAGES) & 1, abort_flag, 10, k);
                 if (!ok) break;
-                fence_async_proxy();  // cp.async writes (generic proxy) must be visible to the tensor pipe's reads
                 tc_fence_after();
                 const uint32_t kb = sK + (idx % KSTAGES) * ITEM_BYTES;
                 const uint32_t d = tmem + TM_S + b * 128;
@@ -837,7 +798,6 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     }
 }
 
-static_assert(sizeof(Item) <= ITEM_SLOT, "item slot too small");
 }  // namespace tc5
 
 bool tc5_eligible(int group, int head_dim) { return head_dim == 128 && group >= 1 && group <= 128; }
@@ -920,39 +880,33 @@ int launch_decode_tc5(const DecodeArgs& a_in, cudaStream_t st) {
     DecodeArgs a = a_in;
     tc5::TmaMaps maps;
     memset(&maps, 0, sizeof(maps));
-    // TMA serves tiles of 128 cached keys when a tile is a whole number of equal boxes: the page size is a
-    // multiple of 128 rows, or divides 128 and is a multiple of the 8-row swizzle period.
-    a.tma_box_rows = 0;
-    a.tma_lvl0 = 0;
+    // Every tile comes by TMA (the caller has checked that page size and strides allow it).  Largest cache box:
+    // min(128, page size) rows.  Without a cache no cache box is ever issued.
+    if (a.max_blocks == 0) a.page_size = 128;
     const int ps = a.page_size;
-    const bool fits = a.max_blocks > 0 && a.num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
-    const bool strides_ok = a.token_stride * 2 % 16 == 0 && a.page_stride * 2 % 16 == 0 &&
-                            a.page_stride * 2 < (1ll << 40) && a.num_pages < (1ll << 31);
-    if (fits && strides_ok) {
-        const int rows = ps < 128 ? ps : 128;
-        int lvl0 = 0;
-        while ((128 >> lvl0) > rows) ++lvl0;
-        for (int lvl = lvl0; lvl < 5; ++lvl) {   // boxes of 128 >> lvl rows: whole tiles use lvl0, tail tiles all of them
-            MapKey kk{a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 128 >> lvl};
-            MapKey kv{a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, 128 >> lvl};
-            int rc = cache_map(kk, &maps.k[lvl]);
-            if (rc == DLX_OK) rc = cache_map(kv, &maps.v[lvl]);
-            if (rc != DLX_OK) return rc;
-        }
-        a.tma_box_rows = rows;
-        a.tma_lvl0 = lvl0;
-    }
-    // Q blocks of 128 / group whole tokens: one box {64, group, tokens} per head_dim half
+    a.tma_box_rows = ps < 128 ? ps : 128;
+    a.tma_lvl0 = 0;
+    while ((128 >> a.tma_lvl0) > a.tma_box_rows) ++a.tma_lvl0;
     a.q_tokens = 128 / a.group;
-    a.q_by_tma = 0;
-    if (a.total_q > 0 && a.q_rs * 2 % 16 == 0 && a.q_rs * 2 < (1ll << 40)) {
-        MapKey kq{a.q, a.q_rs, 0, a.total_q, a.hq, a.group, a.q_tokens, 3};
-        const int rc = cache_map(kq, &maps.q);
+    for (int lvl = 0; lvl < tc5::LEVELS; ++lvl) {
+        const int rows = 128 >> lvl;
+        int rc = DLX_OK;
+        if (rows <= ps && a.max_blocks > 0) {   // caches: a box lies inside one page
+            rc = tc5::tc5_cache_map(a.k_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows, 4, &maps.kc[lvl]);
+            if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows, 4, &maps.vc[lvl]);
+        }
+        // in-flight rows: {head_dim, Hkv, token}, box {64, 1, rows}
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.k, a.k_rs, 0, a.total_kv, a.hkv, 1, rows, 3, &maps.kn[lvl]);
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v, a.v_rs, 0, a.total_kv, a.hkv, 1, rows, 3, &maps.vn[lvl]);
         if (rc != DLX_OK) return rc;
-        a.q_by_tma = 1;
     }
+    {   // Q blocks of 128 / group whole tokens: one box {64, group, tokens} per head_dim half
+        const int rc = tc5::tc5_cache_map(a.q, a.q_rs, 0, a.total_q, a.hq, a.group, a.q_tokens, 3, &maps.q);
+        if (rc != DLX_OK) return rc;
+    }
+    a.q_by_tma = 1;
     // Persistent CTAs: one per bin of the schedule (one per SM, fewer when there is less work).
-    dim3 grid((unsigned)a.bins), block(tc5::NUM_THREADS);
+    dim3 grid((unsigned)(a.bins * a.group_ctas)), block(tc5::NUM_THREADS);
     tc5::decode_attn_tc5_kernel<<<grid, block, tc5::SMEM_BYTES, st>>>(a, maps);
     return check_launch("decode_attn_tc5_kernel");
 }

@@ -60,8 +60,8 @@ constexpr int K_REGION = K_ROWS * 128;       // [64 keys][64 bf16]: 8 KiB
 constexpr int K_STAGE = 2 * K_REGION;        // two head_dim halves
 constexpr int V_STAGE = TILE_N * 128;        // [128 keys][this CTA's 64 head_dim columns]: 16 KiB
 #ifndef DLX_PAIR_KSTAGES
-#define DLX_PAIR_KSTAGES 4
-#define DLX_PAIR_VSTAGES 3
+#define DLX_PAIR_KSTAGES 3
+#define DLX_PAIR_VSTAGES 4
 #endif
 constexpr int KSTAGES = DLX_PAIR_KSTAGES, VSTAGES = DLX_PAIR_VSTAGES;
 static_assert(KSTAGES >= 2 && KSTAGES <= 4 && VSTAGES >= 2 && VSTAGES <= 4, "ring depth");
@@ -79,8 +79,8 @@ constexpr int OFF_ITEMS = OFF_ROWMAP + 128 * 8;
 constexpr int OFF_FLAGS = OFF_ITEMS + MAX_ROUNDS * (int)sizeof(SchedRec);   // redo bit per round
 constexpr int FLAG_WORDS = 128;                    // 4096 rounds
 constexpr int OFF_ARGS = OFF_FLAGS + FLAG_WORDS * 4;
-constexpr int SMEM_BYTES = OFF_ARGS + 256 + 1024;  // + slack for 1024-byte alignment
-static_assert(sizeof(DecodeArgs) <= 256, "argument block copy");
+constexpr int SMEM_BYTES = OFF_ARGS + 320 + 1024;  // + slack for 1024-byte alignment
+static_assert(sizeof(DecodeArgs) <= 320, "argument block copy");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 constexpr int NUM_THREADS = 512;
@@ -88,7 +88,12 @@ constexpr int SOFTMAX_REGS = 184, HELPER_REGS = 56, EPI_REGS = 88;
 static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget");
 constexpr int EPI_WARP0 = 12;
 constexpr int KLOAD_WARP = 8, VLOAD_WARP = 9, QK_WARP = 10, PV_WARP = 11;
-constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384;
+// TMEM columns (512 per CTA): three score buffers of 128 fp32 columns, then O.  P of a tile (128 bf16 = 64 columns)
+// overwrites the first half of the tile's own score buffer once the scores are in registers, so a buffer is busy from
+// the tile's Q K^T until its P V has run, and three tiles are in flight at any time: the chain Q K^T -> scores to
+// registers -> exponentials -> P -> P V is about three tile times long.
+constexpr int NBUF = 3;
+constexpr uint32_t TM_S = 0, TM_O = 384;
 
 // barrier slots (8 bytes each) at OFF_BAR
 enum {
@@ -99,15 +104,14 @@ enum {
     B_KFULLP = 10,   // [stage] even CTA: the odd CTA's half has landed
     B_KEMPTY = 14,   // [stage] both (commit)
     B_VFULL = 18, B_VFULLP = 22, B_VEMPTY = 26,
-    B_SFULL = 30,    // [S buffer] both (commit)
-    B_SFREE = 32,    // [S buffer] even CTA, 8 arrivals: both CTAs' warpgroup has the scores in registers
-    B_PFULL = 34,    // [P buffer] even CTA, 8 arrivals: both CTAs' P is in TMEM
-    B_PFREE = 36,    // [P buffer] both (commit)
-    B_OFULL = 38,    // both (commit)
-    B_OFREE = 39,    // even CTA, 8 arrivals: both epilogue warpgroups hold O in registers
-    B_MRFULL = 40, B_MREMPTY = 42, B_LSFULL = 44, B_LSEMPTY = 46,   // local rings between the warpgroups
-    B_EPIDONE = 48,  // local, 128 arrivals: the epilogue warpgroup has written its last output row
-    B_COUNT = 49
+    B_SFULL = 30,    // [buffer] both (commit): the tile's scores are in TMEM
+    B_PFULL = 33,    // [buffer] even CTA, 8 arrivals: both CTAs' P is in TMEM (over the scores)
+    B_BUFFREE = 36,  // [buffer] even CTA (commit): the tile's P V has run, the next Q K^T may overwrite the buffer
+    B_OFULL = 39,    // both (commit)
+    B_OFREE = 40,    // even CTA, 8 arrivals: both epilogue warpgroups hold O in registers
+    B_MRFULL = 41, B_MREMPTY = 43, B_LSFULL = 45, B_LSEMPTY = 47,   // local rings between the warpgroups
+    B_EPIDONE = 49,  // local, 128 arrivals: the epilogue warpgroup has written its last output row
+    B_COUNT = 50
 };
 static_assert(8 * B_COUNT + 16 <= 512, "barrier block");
 
@@ -189,7 +193,7 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
         // every thread of one / two warpgroups of this CTA, 1 = one thread, a tcgen05.commit or a loader's lane 0
         const int b = tid;
         int count = 1;
-        if (b == B_SFREE || b == B_SFREE + 1 || b == B_PFULL || b == B_PFULL + 1 || b == B_OFREE) count = 8;
+        if ((b >= B_PFULL && b < B_PFULL + NBUF) || b == B_OFREE) count = 8;
         else if (b == B_LSFULL || b == B_LSFULL + 1) count = 256;
         else if (b >= B_MRFULL) count = 128;   // MRFULL, MREMPTY, LSEMPTY, EPIDONE
         mbar_init(bar(b), count);
@@ -243,7 +247,6 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
         const int w = warp >> 2;
         const int L = tid & 127;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const uint32_t tS = lane_base + TM_S + w * 128, tP = lane_base + TM_P + w * 64;
         float* xm = reinterpret_cast<float*>(gbase + OFF_XCH);    // [2][128] row references
         float* xs = xm + 256;                                     // [2][3][128] row sums of each warpgroup, reference
         const float sl2 = a.scale_log2;
@@ -276,8 +279,9 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
             bool out_of_range = false;
 #pragma unroll 1
             for (int jj = jj_first; jj < n && alive; jj += 2) {
-                const int u = (ck + jj) >> 1;
-                bool ok = mbar_wait(bar(B_SFULL + w), u & 1, abort_flag, 1 + w, jj);
+                const int buf = (ck + jj) % NBUF, u = (ck + jj) / NBUF;   // score buffer of the tile and its use count
+                const uint32_t tS = lane_base + TM_S + buf * 128;
+                bool ok = mbar_wait(bar(B_SFULL + buf), u & 1, abort_flag, 1 + w, jj);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
                 if (multi && jj == 0 && mr >= 2) {
@@ -289,9 +293,6 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(bar0(B_SFREE + w));   // the next Q K^T into this buffer may start
                     float mx_any = -INFINITY;
                     if (key0 + TILE_N > it.full_until) {
                         // The tile touches a mask boundary (warp-uniform; one or two tiles per item): hidden scores become
@@ -332,37 +333,22 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                         m_ref = xm[slot * 128 + L];
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    // P = exp2(s * scale - m_ref) as bf16.  The first half of the row is kept in registers: the exponentials
-                    // do not need the P buffer, only the stores do, and half a row later the P V that last read the
-                    // buffer has run (waiting for it up front would stall here, a whole row in registers costs too many)
+                    // P = exp2(s * scale - m_ref) as bf16, written over the first half of the tile's own score buffer (the
+                    // scores are all in registers by now)
                     float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
                     const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(-m_ref, -m_ref);
-                    uint32_t pk[2][16];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t pc[16];
+                        uint32_t pk[16];
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c][e]), __uint_as_float(v[c][e + 1])), sl2v, negm);
                             const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
                             if ((e >> 1) & 1) lacc1 = __fadd2_rn(lacc1, p); else lacc0 = __fadd2_rn(lacc0, p);
-                            if (c < 2) pk[c][e >> 1] = pack2<__nv_bfloat16>(p.x, p.y); else pc[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
+                            pk[e >> 1] = pack2<__nv_bfloat16>(p.x, p.y);
                         }
-                        if (c == 1) {
-                            if (u >= 1) {
-                                // Q K^T does not wait for P V, so this warpgroup could lap the tensor pipe: the previous P in
-                                // this buffer must have been consumed before the next one goes in
-                                bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                                if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                                tc_fence_after();
-                            }
-                            tmem_st16(tP, pk[0]);
-                            tmem_st16(tP + 16, pk[1]);
-                        } else if (c >= 2) {
-                            tmem_st16(tP + c * 16, pc);
-                        }
+                        tmem_st16(tS + c * 16, pk);
                     }
-                    if (!alive) break;
                     lacc0 = __fadd2_rn(lacc0, lacc1);
                     const float tsum = lacc0.x + lacc0.y;
                     out_of_range |= !(tsum <= DLX_SUM_HIGH);   // also catches NaN
@@ -375,16 +361,10 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                         if (!__all_sync(0xffffffffu, okm)) { alive = false; break; }
                         mbar_arrive(bar(B_MREMPTY + slot));
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(bar0(B_SFREE + w));
-                    if (u >= 1) {
-                        bool okp = mbar_wait(bar(B_PFREE + w), (u - 1) & 1, abort_flag, 4, jj);
-                        if (!__all_sync(0xffffffffu, okp)) { alive = false; break; }
-                    }
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(bar0(B_PFULL + w));
+                if (lane == 0) mbar_arrive_cluster(bar0(B_PFULL + buf));
             }
             if (!alive) break;
             if (__any_sync(0xffffffffu, out_of_range && row_valid) && lane == 0)
@@ -733,21 +713,21 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     if (k == 0) prefetch_upto(done + 2);   // the next item's Q, into the other buffer
                 }
             } else {
-                ok = mbar_wait_cluster(bar(B_QFULLP + qb), (done >> 1) & 1, abort_flag, 7, -6);
+                ok = mbar_wait(bar(B_QFULLP + qb), (done >> 1) & 1, abort_flag, 7, -6);
                 if (!ok) break;
                 const uint32_t qaddr = sQ + qb * Q_BYTES;
 #pragma unroll 1
                 for (int k = 0; k < n && ok; ++k) {
                     const int idx = ck + k;
-                    const int b = idx & 1, u = idx >> 1;
+                    const int b = idx % NBUF, u = idx / NBUF;   // score buffer and its use count
                     const int st = idx % KSTAGES;
                     const uint32_t par = (idx / KSTAGES) & 1;
-                    if (u >= 1) {
-                        ok = mbar_wait_cluster(bar(B_SFREE + b), (u - 1) & 1, abort_flag, 11, k);
+                    if (u >= 1) {   // the P V of the tile that used the buffer before must have run
+                        ok = mbar_wait(bar(B_BUFFREE + b), (u - 1) & 1, abort_flag, 11, k);
                         if (!ok) break;
                     }
                     ok = mbar_wait(bar(B_KFULL + st), par, abort_flag, 10, k);
-                    ok = ok && mbar_wait_cluster(bar(B_KFULLP + st), par, abort_flag, 13, k);
+                    ok = ok && mbar_wait(bar(B_KFULLP + st), par, abort_flag, 13, k);
                     if (!ok) break;
                     tc_fence_after();   // K, V and Q were written by TMA copies: the async proxy already sees them
                     const uint32_t kb = sK + st * K_STAGE;
@@ -788,25 +768,25 @@ decode_attn_tc5_pair_kernel(const DecodeArgs a_param, const __grid_constant__ Tm
                     mbar_arrive_cluster(bar0(B_VFULLP + idx % VSTAGES));
                 }
             } else {
-                if (done > 0) ok = mbar_wait_cluster(bar(B_OFREE), (done - 1) & 1, abort_flag, 8, -2);
+                if (done > 0) ok = mbar_wait(bar(B_OFREE), (done - 1) & 1, abort_flag, 8, -2);
 #pragma unroll 1
                 for (int k = 0; k < n && ok; ++k) {
                     const int idx = ck + k;
-                    const int b = idx & 1, u = idx >> 1;
+                    const int b = idx % NBUF, u = idx / NBUF;
                     const int st = idx % VSTAGES;
                     const uint32_t par = (idx / VSTAGES) & 1;
                     ok = mbar_wait(bar(B_VFULL + st), par, abort_flag, 8, k);
-                    ok = ok && mbar_wait_cluster(bar(B_VFULLP + st), par, abort_flag, 14, k);
-                    ok = ok && mbar_wait_cluster(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
+                    ok = ok && mbar_wait(bar(B_VFULLP + st), par, abort_flag, 14, k);
+                    ok = ok && mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                     if (!ok) break;
                     tc_fence_after();   // K, V and Q were written by TMA copies: the async proxy already sees them
                     const uint32_t vb = sV + st * V_STAGE;
-                    const uint32_t pa = tmem + TM_P + b * 64;
+                    const uint32_t pa = tmem + TM_S + b * 128;   // P lies over the first 64 columns of the score buffer
                     const uint64_t dv = smem_desc(vb, V_STAGE, 1024);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
                         mma_ts_pair(tmem + TM_O, pa + kk * 8, dv + (uint64_t)(kk * 2048 / 16), ID_PV, (k > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit_pair(bar(B_PFREE + b));
+                    tc_commit_local(bar(B_BUFFREE + b));
                     tc_commit_pair(bar(B_VEMPTY + st));
                 }
                 if (ok) tc_commit_pair(bar(B_OFULL));
@@ -877,8 +857,8 @@ int launch_decode_tc5_pair(const DecodeArgs& a_in, cudaStream_t st) {
             if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v_cache, a.page_stride, a.token_stride, a.num_pages, a.hkv, ps, rows, 4, &maps.vc[lvl]);
         }
         // in-flight rows: {head_dim, Hkv, token}, box {64, 1, rows}
-        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.k, a.k_rs, 0, a.total_q, a.hkv, 1, rows, 3, &maps.kn[lvl]);
-        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v, a.v_rs, 0, a.total_q, a.hkv, 1, rows, 3, &maps.vn[lvl]);
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.k, a.k_rs, 0, a.total_kv, a.hkv, 1, rows, 3, &maps.kn[lvl]);
+        if (rc == DLX_OK) rc = tc5::tc5_cache_map(a.v, a.v_rs, 0, a.total_kv, a.hkv, 1, rows, 3, &maps.vn[lvl]);
         if (rc != DLX_OK) return rc;
     }
     {

@@ -208,7 +208,9 @@ int device_sm_count() {
     return sms;
 }
 
-void tc5_plan_items(DecodeArgs& a, bool pair, int sm_count) {
+void tc5_plan_items(DecodeArgs& a, bool two_ctas, int sm_count) {
+    const bool pair = two_ctas;
+    a.group_ctas = two_ctas ? 2 : 1;
     a.q_tokens = 128 / a.group;
     a.tokens_per_item = pair ? 2 * a.q_tokens : a.q_tokens;
     const int q_len = a.max_q_len > (1 << 20) ? (1 << 20) : a.max_q_len;

@@ -30,7 +30,7 @@ static int validate_decode(const dlx_decode_attn_params* p) {
     if (p->dtype != DLX_DTYPE_BF16) return fail(DLX_ERR_UNSUPPORTED, "decode: only bf16 is built");
     if (p->head_dim != 64 && p->head_dim != 128)
         return fail(DLX_ERR_UNSUPPORTED, "decode: head_dim %d (64 and 128 are built)", p->head_dim);
-    if (p->num_seqs < 0 || p->total_q < 0 || p->max_blocks < 0 || p->num_pages < 0)
+    if (p->num_seqs < 0 || p->total_q < 0 || p->total_kv < 0 || p->max_blocks < 0 || p->num_pages < 0)
         return fail(DLX_ERR_INVALID_ARGUMENT, "decode: negative count");
     if (p->num_q_heads <= 0 || p->num_kv_heads <= 0 || p->num_q_heads % p->num_kv_heads != 0)
         return fail(DLX_ERR_INVALID_ARGUMENT, "decode: %d query heads over %d KV heads", p->num_q_heads,
@@ -50,13 +50,17 @@ static int validate_decode(const dlx_decode_attn_params* p) {
     return DLX_OK;
 }
 
-// The CTA-pair kernel fetches every cached tile by TMA: page sizes that tile into 64- and 128-row boxes, 16-byte strides.
-static bool pair_supported(const dlx_decode_attn_params* p) {
+// The tcgen05 kernels fetch every tile by TMA: page sizes that tile into boxes of 8..128 rows, 16-byte strides below
+// 2^40 bytes.  Without a cache (max_blocks == 0) only q / k / v count.
+static bool tma_supported(const dlx_decode_attn_params* p) {
     const int ps = p->page_size;
-    const bool fits = p->max_blocks > 0 && p->num_pages > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
+    const bool fits = p->num_pages > 0 && ps > 0 && ((ps % 128 == 0) || (128 % ps == 0 && ps % 8 == 0));
     const bool strides_ok = p->cache_token_stride * 2 % 16 == 0 && p->cache_page_stride * 2 % 16 == 0 &&
                             p->cache_page_stride * 2 < (1ll << 40) && p->num_pages < (1ll << 31);
-    return fits && strides_ok && p->total_q > 0 && p->q_row_stride * 2 % 16 == 0 && p->q_row_stride * 2 < (1ll << 40);
+    const bool rows_ok = p->q_row_stride * 2 % 16 == 0 && p->q_row_stride * 2 < (1ll << 40) &&
+                         p->k_row_stride * 2 % 16 == 0 && p->k_row_stride * 2 < (1ll << 40) &&
+                         p->v_row_stride * 2 % 16 == 0 && p->v_row_stride * 2 < (1ll << 40);
+    return (p->max_blocks == 0 || (fits && strides_ok)) && p->total_q > 0 && rows_ok;
 }
 
 static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
@@ -68,6 +72,7 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     a.q_rs = p->q_row_stride; a.k_rs = p->k_row_stride; a.v_rs = p->v_row_stride; a.o_rs = p->out_row_stride;
     a.page_stride = p->cache_page_stride; a.token_stride = p->cache_token_stride;
     a.bt_stride = p->block_table_stride; a.num_pages = p->num_pages;
+    a.total_kv = p->total_kv > 0 ? p->total_kv : p->total_q;
     a.total_q = p->total_q; a.num_seqs = p->num_seqs; a.max_blocks = p->max_blocks; a.max_q_len = p->max_q_len;
     a.hq = p->num_q_heads; a.hkv = p->num_kv_heads; a.group = a.hq / a.hkv; a.page_size = p->page_size;
     a.mask_mode = p->mask_mode; a.dbs = p->diffusion_block_size > 0 ? p->diffusion_block_size : 1;
@@ -76,14 +81,18 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     const int group = a.group;
     const int64_t rows = (int64_t)group * p->max_q_len;
     d.mma = plan_mma((int)(rows > 1 << 20 ? 1 << 20 : rows), p->head_dim);
-    d.use_tc5 = p->kernel != 1 && tc5_eligible(group, p->head_dim);
-    // More than 128 packed rows per (sequence, KV head): two CTAs share every K / V tile (cta_group::2).
-    d.use_pair = d.use_tc5 && p->kernel != 2 && pair_supported(p) && (p->kernel == 3 || rows > 128);
+    d.use_tc5 = p->kernel != 1 && tc5_eligible(group, p->head_dim) && tma_supported(p);
+    // More than 128 packed rows per (sequence, KV head): an item is two row blocks on two CTAs.  The CTA-pair kernel
+    // (cta_group::2: each CTA fetches half of every K / V tile) is taken on request only: measured, both kernels spend
+    // the same time per key tile (the hand-offs between the tensor pipe and the softmax warps bound it, not the
+    // L2 -> SM traffic the pair halves), and the pair pays for its cross-CTA signalling.
+    d.use_pair = d.use_tc5 && p->kernel == 3 && p->max_blocks > 0;
+    const bool two_ctas = d.use_pair || rows > 128;
     const int sms = kNumSMs;
     if (d.use_tc5) {  // persistent CTAs (or CTA pairs) over 128-key tiles
         a.num_splits = 1;
-        tc5_plan_items(a, d.use_pair, sms);
-        d.mma.block_m = d.use_pair ? 256 : 128; d.mma.block_n = 128; d.mma.ctas_per_sm = 1;
+        tc5_plan_items(a, two_ctas, sms);
+        d.mma.block_m = two_ctas ? 256 : 128; d.mma.block_n = 128; d.mma.ctas_per_sm = 1;
         d.mma.m_blocks = a.m_blocks;
     }
     const int64_t max_len = p->max_kv_len > 0 ? p->max_kv_len : (int64_t)p->max_blocks * p->page_size + p->max_q_len;
@@ -94,7 +103,7 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
         // contexts so ragged batches balance.  A split costs one fp32 partial (write + read) of
         // block_m x hd per item, i.e. 2*M/chunk of the chunk's KV bytes: keep chunks >= 40*M keys.
         const int64_t units = (int64_t)p->num_seqs * p->num_kv_heads * d.mma.m_blocks;
-        const int64_t slots = d.use_pair ? sms / 2 : (int64_t)sms * d.mma.ctas_per_sm;
+        const int64_t slots = (d.use_tc5 && two_ctas) ? sms / 2 : (int64_t)sms * d.mma.ctas_per_sm;
         int64_t want = 1;
         if (units > 0 && units < slots) want = (slots + units - 1) / units;
         const int64_t chunk = 40 * (int64_t)d.mma.block_m > 512 ? 40 * (int64_t)d.mma.block_m : 512;
@@ -111,7 +120,7 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     a.num_splits = splits;
     a.m_blocks = d.mma.m_blocks;
     if (d.use_tc5) {
-        tc5_plan_items(a, d.use_pair, sms);
+        tc5_plan_items(a, two_ctas, sms);
         d.sched_bytes = sched_bytes(a.items_total);
     }
     if (splits > 1) {
@@ -230,8 +239,10 @@ extern "C" int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream) {
                     p->q_row_stride % 8 == 0 && p->k_row_stride % 8 == 0 && p->v_row_stride % 8 == 0 &&
                     p->out_row_stride % 8 == 0 && p->cache_page_stride % 8 == 0 && p->cache_token_stride % 8 == 0;
     if (!al) return fail(DLX_ERR_ALIGNMENT, "decode: base pointers must be 16-byte aligned and strides multiples of 8 elements");
-    if (p->kernel == 3 && !pair_supported(p))
-        return fail(DLX_ERR_UNSUPPORTED, "decode: the CTA-pair kernel needs a page size that tiles into 64/128-row boxes");
+    if (p->kernel >= 2 && !tma_supported(p))
+        return fail(DLX_ERR_UNSUPPORTED, "decode: the tcgen05 kernels need a page size that tiles into boxes of 8..128 rows");
+    if (p->kernel == 3 && p->max_blocks == 0)
+        return fail(DLX_ERR_UNSUPPORTED, "decode: the CTA-pair kernel needs a cache");
 
     DecodePlan d = plan_decode(p);
     DecodeArgs& a = d.args;

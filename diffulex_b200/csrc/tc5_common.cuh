@@ -189,6 +189,10 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n"
                  ::"r"(bar), "h"((uint16_t)3) : "memory");
 }
+// ... or only this CTA's barrier.
+__device__ __forceinline__ void tc_commit_local(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
 // kind::f16 instruction descriptor of the pair: fp32 accumulate, bf16 x bf16, M = 256 (128 per CTA), N = 128.
 __host__ __device__ constexpr uint32_t instr_desc_pair(bool b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((128u >> 3) << 17) | ((256u >> 4) << 24);

@@ -128,6 +128,7 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
     if schedule is not None:
         p.schedule, p.schedule_bytes = schedule.data_ptr(), schedule.numel() * schedule.element_size()
     p.total_q, p.num_seqs = total_q, cu_seqlens_q.numel() - 1
+    p.total_kv = k.shape[0]
     p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
     p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
     p.mask_mode, p.diffusion_block_size = mask_mode, diffusion_block_size

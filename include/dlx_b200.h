@@ -141,6 +141,8 @@ typedef struct dlx_decode_attn_params {
     int32_t kernel;              /* 0 = choose; 1 = mma.sync kernel; 2 = tcgen05 kernel, one CTA per item;
                                     3 = tcgen05 kernel, one CTA pair per item (if eligible)            */
     float scale;                 /* softmax scale, hd^-1/2 in every shipped model                      */
+    int32_t total_kv;            /* rows of k / v; 0 = total_q.  Bounds the tcgen05 kernels' copies of
+                                    in-flight rows: rows past it read as zero                           */
 } dlx_decode_attn_params;
 
 /* Bytes of scratch dlx_decode_attn needs for these parameters when it plans itself (split-K partials

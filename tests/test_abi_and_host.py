@@ -90,12 +90,15 @@ def test_split_planning_is_host_only_and_sized_right(lib):
     n = lambda p: lib.dlx_decode_attn_num_splits(ctypes.byref(p))
     ws = lambda p: lib.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
     sb = lambda p: lib.dlx_decode_attn_schedule_bytes(ctypes.byref(p))
-    # 64 seqs x 4 KV heads = 256 items of 224 rows on 74 CTA pairs, contexts <= 2336 keys: one pass; the only
-    # scratch is the schedule (1 KiB of offsets + one 128-byte record per item) when the call plans itself
+    # 64 seqs x 4 KV heads = 256 items of 224 rows (two row blocks on two CTAs) on 74 schedule bins, contexts <= 2336
+    # keys: one pass; the only scratch is the schedule (1 KiB of offsets + one 128-byte record per item) when the
+    # call plans itself
     p = good_params()
     assert n(p) == 1 and sb(p) == 1024 + 256 * 128 and ws(p) == sb(p)
-    # the single-CTA tcgen05 kernel cuts the 224 rows into two items
-    assert sb(good_params(kernel=2)) == 1024 + 512 * 128
+    # both tcgen05 kernels (two neighbouring CTAs / one CTA pair per item) take the same schedule
+    assert sb(good_params(kernel=2)) == sb(p) and sb(good_params(kernel=3)) == sb(p)
+    # a query block of at most 128 packed rows is one item on one CTA
+    assert sb(good_params(max_q_len=16, total_q=1024)) == 1024 + 256 * 128
     # the mma.sync kernel takes no schedule
     assert sb(good_params(kernel=1)) == 0 and ws(good_params(kernel=1)) == 0
     # forced splits: lse [splits, rows] (256-byte padded) + partial O [splits, rows, hd] fp32 + schedule
