@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(C::NT, C::MINB) decode_attn_mma_kernel(const D
     const int q0 = a.cu_q[seq];
     const int qn = a.cu_q[seq + 1] - q0;
     if (qn <= 0 || q0 < 0 || q0 + qn > a.total_q) return;  // padded or inconsistent sequence: no rows
-    const int ctx = max(a.context_lens[seq], 0);
+    const int ctx = a.context_lens != nullptr ? max(a.context_lens[seq], 0) : 0;
     int kv0 = q0, nnew = qn;
     if (a.cu_kv != nullptr) {
         kv0 = a.cu_kv[seq];

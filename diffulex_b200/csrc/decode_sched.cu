@@ -37,7 +37,7 @@ __device__ ItemShape item_shape(const DecodeArgs& a, int item) {
     it.q0 = a.cu_q[it.seq];
     it.qn = a.cu_q[it.seq + 1] - it.q0;
     if (it.qn <= 0 || it.q0 < 0 || it.q0 + it.qn > a.total_q) return it;
-    it.ctx = max(a.context_lens[it.seq], 0);
+    it.ctx = a.context_lens != nullptr ? max(a.context_lens[it.seq], 0) : 0;
     it.kv0 = it.q0; it.nnew = it.qn;
     if (a.cu_kv != nullptr) {
         it.kv0 = a.cu_kv[it.seq];
@@ -144,31 +144,47 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
             __syncthreads();
         }
     }
-    // Longest-processing-time greedy by one warp: every lane keeps the loads of bins lane, lane + 32, ...; per item
-    // a warp-wide minimum finds the least loaded bin (lowest index on ties), whose lane takes the item.
+    // Longest-processing-time greedy by one warp: every lane keeps the loads of bins lane, lane + 32, ... as packed
+    // words (load << 8 | bin), so that one warp-wide minimum per item finds the least loaded bin, lowest index on ties;
+    // that bin's lane takes the item.  The first `bins` items meet empty bins: item i goes to bin i, with no search.
     if (tid < 32) {
         constexpr int PER_LANE = kSchedMaxBins / 32;
+        static_assert(kSchedMaxBins <= 256, "bin index is packed into 8 bits");
         uint32_t load[PER_LANE], count[PER_LANE];
+        int i0 = 0;
 #pragma unroll
-        for (int j = 0; j < PER_LANE; ++j) { load[j] = (lane + 32 * j < bins) ? 0u : 0xffffffffu; count[j] = 0; }
-        for (int i = 0; i < n_items; ++i) {
-            const unsigned long long key = keys[i];
-            const uint32_t c = 0xffffffffu - (uint32_t)(key >> 32);
+        for (int j = 0; j < PER_LANE; ++j) {
+            const int b = lane + 32 * j;
+            load[j] = 0xffffffffu; count[j] = 0;
+            if (b < bins) {
+                uint32_t c = 0;
+                if (b < n_items) {
+                    const unsigned long long key = keys[b];
+                    c = 0xffffffffu - (uint32_t)(key >> 32);
+                    if (c != 0) { keys[b] = ((unsigned long long)((uint32_t)b << 16) << 32) | (uint32_t)key; count[j] = 1; }
+                }
+                load[j] = (c << 8) | (uint32_t)b;
+            }
+        }
+        __syncwarp();
+        i0 = min(bins, n_items);
+        unsigned long long key = i0 < n_items ? keys[i0] : ~0ull;
+        for (int i = i0; i < n_items; ++i) {
+            const unsigned long long cur = key;
+            if (i + 1 < n_items) key = keys[i + 1];   // next item's key, off the critical path
+            const uint32_t c = 0xffffffffu - (uint32_t)(cur >> 32);
             if (c == 0) break;   // the rest have no rows
-            uint32_t best = 0xffffffffu; int bj = 0;
+            uint32_t best = load[0];
 #pragma unroll
-            for (int j = 0; j < PER_LANE; ++j)
-                if (load[j] < best) { best = load[j]; bj = j; }
-            const uint32_t m = __reduce_min_sync(0xffffffffu, best);
-            // among the lanes that hold the minimum, the lowest bin index wins: bins of lane l are l + 32 j
-            const uint32_t cand = (best == m) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
-            const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
-            if (cand == win && best == m) {
+            for (int j = 1; j < PER_LANE; ++j) best = min(best, load[j]);
+            const uint32_t win = __reduce_min_sync(0xffffffffu, best);
+            const uint32_t wb = win & 0xffu;
+            if ((wb & 31u) == (uint32_t)lane) {
 #pragma unroll
                 for (int j = 0; j < PER_LANE; ++j)
-                    if (j == bj) {
-                        keys[i] = ((unsigned long long)((win << 16) | count[j]) << 32) | (uint32_t)key;
-                        load[j] += c; count[j] += 1;
+                    if (j == (int)(wb >> 5)) {
+                        keys[i] = ((unsigned long long)((wb << 16) | count[j]) << 32) | (uint32_t)cur;
+                        load[j] += c << 8; count[j] += 1;
                     }
             }
         }

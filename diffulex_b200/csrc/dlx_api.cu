@@ -67,7 +67,8 @@ static DecodePlan plan_decode(const dlx_decode_attn_params* p) {
     DecodePlan d{};
     DecodeArgs& a = d.args;
     a.q = p->q; a.k = p->k; a.v = p->v; a.k_cache = p->k_cache; a.v_cache = p->v_cache; a.out = p->out;
-    a.block_tables = p->block_tables; a.context_lens = p->context_lens;
+    a.block_tables = p->block_tables;
+    a.context_lens = p->max_blocks > 0 ? p->context_lens : nullptr;   // no cache: every context is empty
     a.cu_q = p->cu_seqlens_q; a.cu_kv = p->cu_seqlens_kv;
     a.q_rs = p->q_row_stride; a.k_rs = p->k_row_stride; a.v_rs = p->v_row_stride; a.o_rs = p->out_row_stride;
     a.page_stride = p->cache_page_stride; a.token_stride = p->cache_token_stride;
@@ -188,7 +189,7 @@ extern "C" int64_t dlx_decode_attn_schedule_bytes(const dlx_decode_attn_params* 
 }
 
 static int check_decode_pointers(const dlx_decode_attn_params* p, bool need_io) {
-    if (!p->context_lens || !p->cu_seqlens_q) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: null pointer");
+    if ((!p->context_lens && p->max_blocks > 0) || !p->cu_seqlens_q) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: null pointer");
     if (need_io && (!p->q || !p->k || !p->v || !p->out)) return fail(DLX_ERR_INVALID_ARGUMENT, "decode: null pointer");
     if (p->max_blocks > 0 && (!p->block_tables || (need_io && (!p->k_cache || !p->v_cache))))
         return fail(DLX_ERR_INVALID_ARGUMENT, "decode: null cache or block table");

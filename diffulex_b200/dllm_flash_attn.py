@@ -104,8 +104,36 @@ def _schedule(md, q, k, k_cache, v_cache, args) -> "torch.Tensor | None":
 
 
 def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-                            attn_metadata) -> torch.Tensor:
-    """Prefill attention is the next operator on the build list; the name exists so that
-    ``diffulex/attention/attn_impl.py:5-10`` imports.  It raises instead of silently computing
-    on another backend."""
-    raise NotImplementedError("dllm_flash_attn_prefill: the sm_100a prefill kernel is not built yet")
+                            attn_metadata, out: "torch.Tensor | None" = None) -> torch.Tensor:
+    """Drop-in body for the reference's prefill attention (dllm_flash_attn_prefill,
+    diffulex_kernel/python/dllm_flash_attn.py:539-596): ``q [sumQ, Hq, hd]``, ``k/v [sumK, Hkv, hd]`` of the
+    prompts themselves, no cache -> ``o [sumQ, Hq, hd]``.
+
+    ``attn_type == "full_attention"``: every key of the sequence is visible (the reference calls a dense
+    non-causal varlen attention, :546-552).  ``"block_attention"``: key j is visible to query i when
+    ``j < (i // diffusion_block_size + 1) * diffusion_block_size`` (the reference's TileLang kernel, :109-116,
+    compiled per shape tuple and autotuned during warm-up, :554-595; here shapes are run-time arguments and
+    there is no hidden ``kernel_config`` state).  ``scale`` is honoured in both modes (the reference kernel
+    hard-codes head_dim**-0.5, :42).  Runs the decode kernels with an empty context: same tiles, same masks."""
+    md = attn_metadata
+    kind = md.attn_type
+    if kind not in ("full_attention", "block_attention"):
+        raise ValueError(f"unknown attn_type {kind!r}")
+    ops._need_cuda(q, k, v)
+    dbs = int(getattr(md, "diffusion_block_size", 0) or 0)
+    if kind == "block_attention" and dbs <= 0:
+        raise ValueError("block_attention needs diffusion_block_size > 0")
+    num_seqs = md.cu_seqlens_q.numel() - 1
+    max_q = int(getattr(md, "max_seqlen_q", 0) or 0) or int(q.shape[0])
+    max_kv = int(getattr(md, "max_seqlen_k", 0) or 0)
+    no_cache = q.new_empty((0, 1, k.shape[1], q.shape[2]))
+    no_tables = md.cu_seqlens_q.new_empty((num_seqs, 0))
+    no_context = md.cu_seqlens_q.new_empty(0)   # ignored without a cache
+    mask = DLX_MASK_BLOCK_CAUSAL if kind == "block_attention" else DLX_MASK_FULL
+    args = (no_tables, no_context, md.cu_seqlens_q, md.cu_seqlens_k, float(scale), max_q, max_kv, mask, dbs,
+            int(getattr(md, "num_splits", 0) or 1))
+    sched = _schedule(md, q, k, no_cache, no_cache, args)
+    if out is None:
+        return ops.decode_attn(q, k, v, no_cache, no_cache, *args, sched)
+    ops.decode_attn_out(out, q, k, v, no_cache, no_cache, *args, sched)
+    return out

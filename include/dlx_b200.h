@@ -103,6 +103,12 @@ int dlx_load_kvcache(const void* k_cache, const void* v_cache, int64_t cache_pag
  * cu_seqlens_kv == NULL to address the in-flight rows with cu_seqlens_q (varlen convention, where
  * the caller's cu_seqlens_k cumulates ctx+new).  Query head h reads KV head h / (Hq/Hkv)
  * (dllm_flash_attn.py:236).  Sequences with a non-positive query length are skipped.
+ *
+ * Prefill (dllm_flash_attn_prefill, dllm_flash_attn.py:539-596) is the same call without a cache:
+ * max_blocks == 0 (caches, block_tables and context_lens may be NULL), cu_seqlens_kv = the prompt's
+ * cu_seqlens_k, mask_mode DLX_MASK_FULL for attn_type "full_attention" (:546-552) and
+ * DLX_MASK_BLOCK_CAUSAL for "block_attention" (key j visible to query i when
+ * j < (i / diffusion_block_size + 1) * diffusion_block_size, :109-116).
  */
 typedef struct dlx_decode_attn_params {
     uint32_t struct_bytes;       /* = sizeof(dlx_decode_attn_params), checked                          */
@@ -114,7 +120,7 @@ typedef struct dlx_decode_attn_params {
     const void* v_cache;
     void* out;                   /* [total_q, Hq, hd], row stride out_row_stride                       */
     const int32_t* block_tables; /* [num_seqs, max_blocks], -1 padded                                  */
-    const int32_t* context_lens; /* [num_seqs]                                                         */
+    const int32_t* context_lens; /* [num_seqs]; ignored (may be NULL) when max_blocks == 0             */
     const int32_t* cu_seqlens_q; /* [num_seqs + 1]                                                     */
     const int32_t* cu_seqlens_kv;/* [num_seqs + 1] in-flight offsets, or NULL (= cu_seqlens_q)         */
     const void* schedule;        /* optional: a schedule written by dlx_decode_attn_prepare for THESE

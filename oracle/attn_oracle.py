@@ -76,3 +76,16 @@ def decode_attention(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_s
         probs = torch.softmax(logits, dim=-1)
         out[q0:q1] = torch.matmul(probs, vs).permute(1, 0, 2)
     return out
+
+
+def prefill_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale: float, is_block_attn: bool,
+                      diffusion_block_size: int = 32) -> torch.Tensor:
+    """fp32 attention of every prompt over its own keys, no cache: the reference's check of its prefill
+    kernel (``naive_sdpa_prefill``, tests/python/kernel/test_dllm_flash_attn_prefill_kernel.py:13-77).
+    ``is_block_attn``: query i sees keys j < (i // dbs + 1) * dbs (:57-62); else every key (:46-55).
+    q [sumQ, Hq, hd]; k, v [sumK, Hkv, hd]; returns fp32 [sumQ, Hq, hd]."""
+    n = cu_seqlens_q.numel() - 1
+    none = k.new_zeros((0, 1, k.shape[1], k.shape[2]))
+    return decode_attention(q, k, v, none, none, torch.zeros((n, 0), dtype=torch.int32),
+                            torch.zeros(n, dtype=torch.int32), cu_seqlens_q, cu_seqlens_k, scale,
+                            MASK_D2F_BLOCK_CAUSAL if is_block_attn else MASK_BD_FULL, diffusion_block_size)

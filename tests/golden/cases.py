@@ -84,6 +84,53 @@ def attn_problem(case: dict):
     return make_problem(case["w"](), device="cpu", values="numpy", permute_pages=case["permute"])
 
 
+# ---- prefill ----------------------------------------------------------------------------------
+def _ref_prefill(seqs, hq, hkv, hd, qlen, block, dbs, seed):
+    return dict(hq=hq, hkv=hkv, hd=hd, q_lens=[qlen] * seqs, kv_lens=[qlen] * seqs, block=block, dbs=dbs, seed=seed)
+
+
+PREFILL_CASES = {
+    # geometries of the reference's own prefill-kernel tests
+    # (tests/python/kernel/test_dllm_flash_attn_prefill_kernel.py:162-310), drawn from a seed
+    "ref_single_seq": _ref_prefill(1, 32, 8, 128, 192, False, 32, 61),
+    "ref_multi_seq": _ref_prefill(4, 32, 8, 128, 256, False, 32, 62),
+    "ref_block_attn": _ref_prefill(2, 32, 8, 128, 256, True, 32, 63),
+    "ref_block_attn_long": _ref_prefill(3, 32, 8, 128, 320, True, 32, 64),
+    "ref_block_attn_dbs64": _ref_prefill(2, 32, 8, 128, 256, True, 64, 65),
+    "ref_gqa_4": _ref_prefill(2, 32, 8, 128, 192, False, 32, 66),
+    "ref_gqa_8": _ref_prefill(2, 32, 4, 128, 192, False, 32, 67),
+    "ref_block_attn_gqa_8": _ref_prefill(2, 32, 4, 128, 256, True, 32, 68),
+    "ref_head_dim_64": _ref_prefill(2, 32, 8, 64, 192, False, 32, 69),
+    "ref_varied_stages": _ref_prefill(2, 32, 8, 128, 192, False, 32, 70),
+    # cases the reference's tests do not pin: ragged prompts (shorter than a key tile, not multiples of the
+    # diffusion block), 7 query heads per KV head, one query head per KV head
+    "ragged_block_gqa7": dict(hq=28, hkv=4, hd=128, q_lens=[100, 33, 257, 1], kv_lens=[100, 33, 257, 1], block=True,
+                              dbs=32, seed=71),
+    "ragged_full_mha": dict(hq=8, hkv=8, hd=128, q_lens=[129, 5, 300], kv_lens=[129, 5, 300], block=False, dbs=32,
+                            seed=72),
+}
+PREFILL_FIXTURE_HEADS = 2     # heads per case kept in the fixture (first and last)
+PREFILL_FIXTURE_ROWS = 192    # rows per case kept in the fixture (seeded choice)
+
+
+def prefill_inputs(case: dict):
+    """(q, k, v, cu_seqlens_q, cu_seqlens_k) of a prefill case: bf16 values drawn with numpy from the seed."""
+    rng = np.random.default_rng([case["seed"], 7])
+    tq, tk = sum(case["q_lens"]), sum(case["kv_lens"])
+    mk = lambda n, h: torch.from_numpy(rng.standard_normal(size=(n, h, case["hd"]), dtype=np.float32)).to(torch.bfloat16)
+    q, k, v = mk(tq, case["hq"]), mk(tk, case["hkv"]), mk(tk, case["hkv"])
+    cu = lambda lens: torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+    return q, k, v, cu(case["q_lens"]), cu(case["kv_lens"])
+
+
+def prefill_fixture_index(case: dict):
+    """(rows, heads) of a case's outputs that the fixture holds."""
+    tq = sum(case["q_lens"])
+    rng = np.random.default_rng([case["seed"], 8])
+    rows = np.sort(rng.choice(tq, size=min(tq, PREFILL_FIXTURE_ROWS), replace=False))
+    return rows, [0, case["hq"] - 1]
+
+
 # ---- store -------------------------------------------------------------------------------------
 STORE_CASES = {
     "cfg1": dict(w=lambda: named_workload("cfg1"), slot_dtype="int32", drop_every=0, row_pad=0),

@@ -18,7 +18,8 @@ copy); attention inputs are the bf16-rounded values widened to fp32.
 
 Outputs: store_golden.json / store_distinct_golden.json / load_golden.json (sha256 digests: bit-exact work needs no more),
 load_written_rows.npz (which rows the reference wrote), attn_golden.npz (fp32 outputs of a few
-heads per case).
+heads per case), prefill_golden.npz (``naive_sdpa_prefill`` on the prefill cases: fp32 outputs of two heads
+and a seeded choice of rows per case).
 """
 from __future__ import annotations
 
@@ -36,8 +37,9 @@ sys.path.insert(0, str(HERE.parent.parent))
 import numpy as np
 import torch
 
-from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, attn_problem, bits, digest,
-                                distinct_caches, load_problem, store_inputs)
+from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, PREFILL_CASES, STORE_CASES, attn_problem, bits,
+                                digest, distinct_caches, load_problem, prefill_fixture_index, prefill_inputs,
+                                store_inputs)
 
 SENTINEL = 1  # int16 bit pattern of a bf16 denormal; N(0,1) draws rounded to bf16 never produce it
 
@@ -142,6 +144,20 @@ def gen_attn(ref_decode_test, ref_prefill_test):
     (HERE / "attn_golden.json").write_text(json.dumps(meta, indent=1))
 
 
+def gen_prefill(ref_prefill_test):
+    meta, arrays = {}, {}
+    for name, case in PREFILL_CASES.items():
+        q, k, v, cu_q, cu_k = prefill_inputs(case)
+        o = ref_prefill_test.naive_sdpa_prefill(q.float(), k.float(), v.float(), cu_q, cu_k, case["hd"] ** -0.5,
+                                                case["dbs"], case["block"])
+        rows, heads = prefill_fixture_index(case)
+        arrays[name] = o[rows][:, heads].numpy().astype(np.float32)
+        meta[name] = dict(inputs=digest(q, k, v, cu_q, cu_k), source="naive_sdpa_prefill")
+        print("prefill", name, arrays[name].shape)
+    np.savez(HERE / "prefill_golden.npz", **arrays)
+    (HERE / "prefill_golden.json").write_text(json.dumps(meta, indent=1))
+
+
 def main():
     ref_root = Path(sys.argv[1]).resolve()
     sys.path.insert(0, str(ref_root))
@@ -153,6 +169,7 @@ def main():
     import test_dllm_flash_attn_decode_kernel as ref_decode_test
     import test_dllm_flash_attn_prefill_kernel as ref_prefill_test
     gen_attn(ref_decode_test, ref_prefill_test)
+    gen_prefill(ref_prefill_test)
 
 
 if __name__ == "__main__":

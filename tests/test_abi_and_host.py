@@ -138,7 +138,10 @@ def test_python_mirror_rejects_bad_inputs_without_a_gpu(lib):
     md.decode_mode = "other"
     with pytest.raises(ValueError):
         dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        dlx.dllm_flash_attn_prefill(p.q, p.k, p.v, p.scale, md)
+    md.attn_type = "other"
+    with pytest.raises(ValueError, match="attn_type"):
         dlx.dllm_flash_attn_prefill(p.q, p.k, p.v, p.scale, md)
 
 
@@ -162,6 +165,56 @@ def test_dropin_package_exposes_reference_names(lib, monkeypatch):
         assert callable(getattr(mod, name))
     sub = importlib.import_module("diffulex_kernel.python.kv_cache_kernels")
     assert callable(sub.load_kvcache)
+
+
+REFERENCE = Path("/root/reference")
+needs_reference = pytest.mark.skipif(not (REFERENCE / "diffulex_kernel").is_dir(),
+                                     reason="the reference checkout is not on this machine")
+
+
+def _reference_signature(path: Path, name: str):
+    """Parameter names of a top-level function of a reference source file, read as text (no import: the file
+    pulls in its JIT compilers at import time)."""
+    import ast
+    for node in ast.parse(path.read_text()).body:
+        if isinstance(node, ast.FunctionDef) and node.name == name:
+            return [a.arg for a in node.args.args]
+    raise AssertionError(f"{name} not found in {path}")
+
+
+@needs_reference
+@pytest.mark.parametrize("module, name", [
+    ("kv_cache_kernels", "store_kvcache_unified_layout"), ("kv_cache_kernels", "store_kvcache_distinct_layout"),
+    ("kv_cache_kernels", "load_kvcache"), ("dllm_flash_attn", "dllm_flash_attn_decode"),
+    ("dllm_flash_attn", "dllm_flash_attn_prefill")])
+def test_entry_points_keep_the_reference_signatures(lib, module, name):
+    """Same positional parameters, same names, same order as the reference's functions; anything this
+    package adds is a keyword with a default."""
+    import inspect
+    import diffulex_b200 as dlx
+    want = _reference_signature(REFERENCE / "diffulex_kernel" / "python" / f"{module}.py", name)
+    params = list(inspect.signature(getattr(dlx, name)).parameters.values())
+    assert [p.name for p in params[:len(want)]] == want
+    assert all(p.default is not inspect.Parameter.empty for p in params[len(want):])
+
+
+@needs_reference
+def test_reference_attention_layer_binds_the_dropin(lib):
+    """With the shadow package ahead of the reference checkout on the path, the reference's own attention layer
+    (diffulex/attention/attn_impl.py:5-10) imports these operators.  Run in a child process: it changes what
+    ``diffulex_kernel`` means."""
+    import os
+    import subprocess
+    import sys
+    code = ("import diffulex.attention.attn_impl as m, diffulex_b200 as d;"
+            "assert m.dllm_flash_attn_decode is d.dllm_flash_attn_decode;"
+            "assert m.dllm_flash_attn_prefill is d.dllm_flash_attn_prefill;"
+            "assert m.store_kvcache_unified_layout is d.store_kvcache_unified_layout;"
+            "assert m.store_kvcache_distinct_layout is d.store_kvcache_distinct_layout;"
+            "import diffulex_kernel.python.kv_cache_kernels as k; assert k.load_kvcache is d.load_kvcache")
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(ROOT / "diffulex_b200" / "dropin"), str(ROOT), str(REFERENCE)]))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
 
 
 # ---- workloads and partition ---------------------------------------------------------------------

@@ -485,8 +485,9 @@ def test_errors_are_raised_before_launch(dlx):
     bad.decode_mode = "paged"
     with pytest.raises(ValueError):
         dlx.dllm_flash_attn_decode(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, pd.scale, bad)
-    with pytest.raises(NotImplementedError):
-        dlx.dllm_flash_attn_prefill(pd.q, pd.k, pd.v, pd.scale, md)
+    bad.attn_type = "causal"
+    with pytest.raises(ValueError):
+        dlx.dllm_flash_attn_prefill(pd.q, pd.k, pd.v, pd.scale, bad)
     # a clean call still works afterwards (no sticky error, context intact)
     o = run_decode(dlx, pd)
     torch.testing.assert_close(o.float().cpu(), oracle_out(p), atol=ATOL, rtol=RTOL)

@@ -7,8 +7,9 @@ import pytest
 import torch
 
 from oracle import attn_oracle, kv_cache_oracle
-from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, STORE_CASES, attn_problem, bits, digest,
-                                distinct_caches, load_problem, store_inputs)
+from tests.golden.cases import (ATTN_CASES, D2F_CASES, LOAD_CASES, PREFILL_CASES, STORE_CASES, attn_problem, bits,
+                                digest, distinct_caches, load_problem, prefill_fixture_index, prefill_inputs,
+                                store_inputs)
 
 
 @pytest.fixture(scope="module")
@@ -92,3 +93,16 @@ def test_attention_oracle_varlen_offsets():
     b = attn_oracle.decode_attention(p.q, p.k, p.v, p.k_cache, p.v_cache, p.block_tables, p.context_lens,
                                      p.cu_seqlens_q, p.cu_seqlens_k_total, p.scale, kv_offsets_from_q=True)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", list(PREFILL_CASES))
+def test_prefill_oracle_matches_reference(name, golden_dir):
+    """The prefill oracle against the reference's own prefill check run on the same seeded prompts."""
+    meta = json.loads((golden_dir / "prefill_golden.json").read_text())[name]
+    want = torch.from_numpy(np.load(golden_dir / "prefill_golden.npz")[name])
+    case = PREFILL_CASES[name]
+    q, k, v, cu_q, cu_k = prefill_inputs(case)
+    assert digest(q, k, v, cu_q, cu_k) == meta["inputs"], "inputs drifted"
+    o = attn_oracle.prefill_attention(q, k, v, cu_q, cu_k, case["hd"] ** -0.5, case["block"], case["dbs"])
+    rows, heads = prefill_fixture_index(case)
+    torch.testing.assert_close(o[rows][:, heads], want, atol=2e-5, rtol=1e-5)
