@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--no-strong", action="store_true", help="skip the cfg5 strong-scaling side measurement")
     ap.add_argument("--no-splitk", action="store_true", help="skip the split-K side measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill side measurement")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU kernels (needs baseline/_ref)")
     ap.add_argument("--no-store-load", action="store_true", help="skip the store / load bandwidth side measurement")
     ap.add_argument("--only-store-load", action="store_true",
                     help="run only the store / load side measurement and print its object (for profiler captures)")
@@ -330,6 +333,135 @@ def splitk_side(dlx, ops, dev, peak):
             "kernels": "decode attention (key-range splits) + combine_splits"}
 
 
+def _graph_us(fn, calls=10, replays=3):
+    """Device time per call of ``fn``, from CUDA-graph replays (events on the current stream)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(calls):
+            fn()
+    graph.replay()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(replays):
+        graph.replay()
+    eb.record()
+    torch.cuda.synchronize()
+    return ea.elapsed_time(eb) / (calls * replays) * 1e3
+
+
+def _eager_us(fn, calls=20):
+    """Device time per call of ``fn`` launched eagerly (for code that cannot be captured: it synchronises)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(calls):
+        fn()
+    eb.record()
+    torch.cuda.synchronize()
+    return ea.elapsed_time(eb) / calls * 1e3
+
+
+def prefill_side(dlx, dev):
+    """Prefill attention (no cache) on prompts of the headline geometry: 8 prompts of 4096 tokens, block-causal
+    with 32-token diffusion blocks and full.  FLOPs = 4 * head_dim * visible (query, key) pairs * query heads."""
+    from types import SimpleNamespace as NS
+    geo = dict(hq=28, hkv=4, hd=128, seqs=8, qlen=4096, dbs=32)
+    tq = geo["seqs"] * geo["qlen"]
+    gen = torch.Generator(device=dev).manual_seed(3)
+    q = torch.randn(tq, geo["hq"], geo["hd"], device=dev, dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(tq, geo["hkv"], geo["hd"], device=dev, dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(tq, geo["hkv"], geo["hd"], device=dev, dtype=torch.bfloat16, generator=gen)
+    cu = torch.arange(0, tq + 1, geo["qlen"], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    res = {"workload": f"{geo['seqs']} prompts x {geo['qlen']} tokens, {geo['hq']}q/{geo['hkv']}kv x {geo['hd']}, "
+                       f"diffusion block {geo['dbs']}", "peak_tflops": tensor_peak_tflops() or 1590.0}
+    for kind in ("block_attention", "full_attention"):
+        md = NS(is_prefill=True, attn_type=kind, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=geo["qlen"],
+                max_seqlen_k=geo["qlen"], diffusion_block_size=geo["dbs"])
+        us = _graph_us(lambda: dlx.dllm_flash_attn_prefill(q, k, v, geo["hd"] ** -0.5, md, out=out), calls=3, replays=3)
+        n, b = geo["qlen"], geo["dbs"]
+        pairs = n * n if kind == "full_attention" else sum(b * (i + 1) * b for i in range(n // b))
+        flops = 4.0 * geo["hd"] * pairs * geo["hq"] * geo["seqs"]
+        res[kind] = {"us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12,
+                     "frac_of_peak": flops / (us * 1e-6) / 1e12 / res["peak_tflops"],
+                     "query_tokens_per_s": tq / (us * 1e-6)}
+    return res
+
+
+def reference_gpu_side(dlx, dev, w):
+    """The reference's OWN GPU kernels (copied unmodified by baseline/make_ref.sh into baseline/_ref) on one layer of
+    the headline workload, next to this package's kernels on the same tensors: Triton store (K4), Triton gather +
+    dense varlen attention (K6 + K7, the reference's varlen decode), TileLang decode kernel (K1, its static decode).
+    A side measurement: the `--impl reference` arm stays the CPU port."""
+    ref_root = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "diffulex_kernel")):
+        return {"unavailable": "baseline/_ref not made (baseline/make_ref.sh)"}
+    import importlib
+    from diffulex_b200.workload import make_problem
+    sys.path.insert(0, ref_root)
+    res = {"workload": f"one layer of {w.name}", "versions": {}}
+    try:
+        for name in ("triton", "tilelang", "flash_attn"):
+            try:
+                res["versions"][name] = getattr(importlib.import_module(name), "__version__", "?")
+            except Exception as e:  # noqa: BLE001
+                res["versions"][name] = f"import failed: {type(e).__name__}: {str(e)[:120]}"
+        kv = importlib.import_module("diffulex_kernel.python.kv_cache_kernels")
+        fa = importlib.import_module("diffulex_kernel.python.dllm_flash_attn")
+        p = make_problem(w, device=dev, values="torch")
+        kvb = p.kv_bytes()
+        out = torch.empty_like(p.q)
+        md_s, md_v = p.metadata("static"), p.metadata("varlen")
+
+        def entry(us):
+            return {"us": us, "kv_gbps": kvb / (us * 1e-6) / 1e9}
+        ours = {"store_us": _graph_us(lambda: dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, p.slot_mapping, md_s)),
+                "decode_static": entry(_graph_us(lambda: dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_s, out=out))),
+                "decode_varlen": entry(_graph_us(lambda: dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_v, out=out)))}
+        theirs = {}
+        try:
+            theirs["store_us"] = _graph_us(lambda: kv.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, p.slot_mapping, md_s))
+        except Exception as e:  # noqa: BLE001
+            theirs["store_us"] = f"failed: {type(e).__name__}: {str(e)[:200]}"
+        try:   # its gather sizes the output from a device value (a host sync): eager launches, device-timed
+            theirs["decode_varlen"] = entry(_eager_us(lambda: fa.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_v)))
+            theirs["decode_varlen"]["kernels"] = "Triton load_kvcache + flash_attn_varlen_func"
+        except Exception as e:  # noqa: BLE001
+            theirs["decode_varlen"] = f"failed: {type(e).__name__}: {str(e)[:200]}"
+        best = None
+        tried = {}
+        # the reference autotunes 54 tile configurations during warm-up; a few of them here, best kept
+        for cfg in ((64, 64, 1, 128), (64, 128, 2, 128), (128, 64, 2, 256), (128, 128, 2, 256)):
+            fa.kernel_config = dict(BLOCK_M=cfg[0], BLOCK_N=cfg[1], NUM_STAGES=cfg[2], NUM_THREADS=cfg[3])
+            try:
+                o = fa.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_s)
+                ok = bool(torch.allclose(o.float(), dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_s).float(),
+                                         atol=2e-2, rtol=1e-2))
+                us = _eager_us(lambda: fa.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md_s))
+                tried["x".join(map(str, cfg))] = {"us": us, "agrees_with_ours": ok}
+                if ok and (best is None or us < best):
+                    best = us
+            except Exception as e:  # noqa: BLE001
+                tried["x".join(map(str, cfg))] = f"failed: {type(e).__name__}: {str(e)[:160]}"
+        theirs["decode_static"] = dict(entry(best), kernels="TileLang dllm_flash_attn_decode_kernel",
+                                       configs=tried) if best else {"configs": tried}
+        res["ours"], res["reference"] = ours, theirs
+        if best:
+            res["decode_static_speedup"] = best / ours["decode_static"]["us"]
+        if isinstance(theirs.get("decode_varlen"), dict):
+            res["decode_varlen_speedup"] = theirs["decode_varlen"]["us"] / ours["decode_varlen"]["us"]
+    except Exception as e:  # noqa: BLE001
+        res["unavailable"] = f"{type(e).__name__}: {str(e)[:300]}"
+    finally:
+        sys.path.remove(ref_root)
+    return res
+
+
 def run_reference(args, w, rank, world):
     """The reference's CPU implementation of the path (its PyTorch attention check, restated in
     oracle/attn_oracle.py; the reference itself is Python and cannot travel) on the host cores."""
@@ -458,10 +590,19 @@ def main():
         for p in layers:
             dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
     torch.cuda.current_stream().wait_stream(side)
+    # The step's schedule is planned once, outside this graph (in the step graph above the planning launch is inside):
+    # what is timed here is the attention kernel (and the combine kernel when the plan splits), nothing else.
+    from diffulex_b200._lib import DLX_MASK_BLOCK_CAUSAL, DLX_MASK_FULL
+    p0 = layers[0]
+    dec_args = (md.block_tables, md.context_lens, md.cu_seqlens_q, md.cu_seqlens_k, float(p0.scale),
+                int(md.max_seqlen_q), 0, DLX_MASK_BLOCK_CAUSAL if md.mask_mode == "d2f_block_causal" else DLX_MASK_FULL,
+                int(md.diffusion_block_size), int(getattr(md, "num_splits", 0) or 0))
+    sched = ops.decode_schedule(p0.q, p0.k, p0.k_cache, p0.v_cache, *dec_args)
+    dec_outs = [torch.empty_like(p.q) for p in layers]
     g_dec = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_dec):
-        for p in layers:
-            dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+        for p, o in zip(layers, dec_outs):
+            ops.decode_attn_out(o, p.q, p.k, p.v, p.k_cache, p.v_cache, *dec_args, sched)
     for _ in range(3):
         g_dec.replay()
     evs = []
@@ -582,7 +723,7 @@ def main():
         }
 
     # ---- side measurements: the cfg2 state is released first ----
-    del layers, graph, g_dec, base
+    del layers, graph, g_dec, base, dec_outs
     if e2e is not None:
         del h_q, h_k, h_v, h_out, d_q, d_k, d_v, d_out
     torch.cuda.empty_cache()
@@ -599,6 +740,14 @@ def main():
     if rank == 0 and world == 1 and not args.no_store_load:
         store_load = store_load_bandwidth(dlx, dev, peak, args.store_load_seqs)
 
+    prefill = None
+    if rank == 0 and world == 1 and not args.no_prefill:
+        prefill = prefill_side(dlx, dev)
+        torch.cuda.empty_cache()
+    reference_gpu = None
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        reference_gpu = reference_gpu_side(dlx, dev, w_global)
+        torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, toks, cores, sample = cpu_attention_baseline(w_global)
@@ -623,7 +772,8 @@ def main():
                              f"{kv_bytes_layer * L / 1e9:.2f} GB of KV per step",
                        "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.scaling})")},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "host_us_per_call": host_cost,
-            "strong_cfg5": strong, "splitk": splitk, "store_load": store_load,
+            "strong_cfg5": strong, "splitk": splitk, "store_load": store_load, "prefill": prefill,
+            "reference_gpu": reference_gpu,
             # per step: L x (store + decode [+ combine]) + the one planning launch of the step's schedule
             "gpu_launches": args.steps * (L * launches_per_layer + 1), "clocks": clocks, "per_rank_ms": per_rank_ms,
         }

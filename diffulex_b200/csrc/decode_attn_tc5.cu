@@ -813,10 +813,21 @@ struct MapKey {   // cache map: as named; Q map: (q, row stride, 0, total_q, Hq,
                num_pages == o.num_pages && hkv == o.hkv && page_size == o.page_size && rows == o.rows && rank == o.rank;
     }
 };
-struct MapEntry { MapKey key; CUtensorMap map; };
+struct MapEntry { MapKey key; CUtensorMap map; bool used = false; };
+// Memo: a hashed table with short probe runs; a launch looks up a few dozen maps, so a lookup has to cost
+// nanoseconds however many layers' caches are in it.  A full run of probes replaces one of its entries.
+constexpr size_t MAP_SLOTS = 4096, MAP_PROBES = 8;
 std::mutex g_map_mutex;
 std::vector<MapEntry> g_maps;
 size_t g_map_next = 0;
+inline size_t map_hash(const MapKey& k) {
+    uint64_t h = 0x9e3779b97f4a7c15ull;
+    auto mix = [&h](uint64_t v) { h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2); };
+    mix(reinterpret_cast<uint64_t>(k.ptr) >> 4); mix((uint64_t)k.page_stride); mix((uint64_t)k.token_stride);
+    mix((uint64_t)k.num_pages); mix(((uint64_t)(uint32_t)k.hkv << 32) | (uint32_t)k.page_size);
+    mix(((uint64_t)(uint32_t)k.rows << 8) | (uint32_t)k.rank);
+    return (size_t)(h ^ (h >> 29));
+}
 typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                              const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -833,14 +844,21 @@ EncodeFn encode_fn() {
 }
 int cache_map(const MapKey& k, CUtensorMap* out) {
     std::lock_guard<std::mutex> lock(g_map_mutex);
-    for (const MapEntry& e : g_maps)
-        if (e.key == k) { *out = e.map; return DLX_OK; }
+    if (g_maps.empty()) g_maps.resize(MAP_SLOTS);
+    const size_t h = map_hash(k);
+    size_t slot = MAP_SLOTS;
+    for (size_t i = 0; i < MAP_PROBES; ++i) {
+        MapEntry& e = g_maps[(h + i) & (MAP_SLOTS - 1)];
+        if (e.used && e.key == k) { *out = e.map; return DLX_OK; }
+        if (!e.used && slot == MAP_SLOTS) slot = (h + i) & (MAP_SLOTS - 1);
+    }
+    if (slot == MAP_SLOTS) slot = (h + (g_map_next++ % MAP_PROBES)) & (MAP_SLOTS - 1);
     EncodeFn enc = encode_fn();
     if (enc == nullptr) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from this driver");
     cuuint64_t gdim[4] = {(cuuint64_t)tc5::HD, (cuuint64_t)k.hkv, (cuuint64_t)k.page_size, (cuuint64_t)k.num_pages};
     cuuint64_t gstr[3] = {(cuuint64_t)tc5::HD * 2, (cuuint64_t)k.token_stride * 2, (cuuint64_t)k.page_stride * 2};
     cuuint32_t box[4] = {64, 1, (cuuint32_t)k.rows, 1};
-    if (k.rank == 3) {   // Q: {head_dim, Hq, token}, box {64, group, tokens per block}
+    if (k.rank == 3) {   // Q and in-flight rows: {head_dim, heads, token}, box {64, heads per box, tokens per box}
         gdim[2] = (cuuint64_t)k.num_pages;
         gstr[1] = (cuuint64_t)k.page_stride * 2;
         box[1] = (cuuint32_t)k.page_size; box[2] = (cuuint32_t)k.rows;
@@ -848,12 +866,12 @@ int cache_map(const MapKey& k, CUtensorMap* out) {
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     MapEntry e;
     e.key = k;
+    e.used = true;
     const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)k.rank, const_cast<void*>(k.ptr), gdim, gstr, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(DLX_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
-    if (g_maps.size() < 512) g_maps.push_back(e);
-    else { g_maps[g_map_next] = e; g_map_next = (g_map_next + 1) % g_maps.size(); }
+    g_maps[slot] = e;
     *out = e.map;
     return DLX_OK;
 }

@@ -59,28 +59,33 @@ __device__ ItemShape item_shape(const DecodeArgs& a, int item) {
 }
 
 __device__ void write_record(const DecodeArgs& a, const ItemShape& it, SchedRec* out) {
-    SchedRec r;
-    r.seq = it.seq; r.kvh = it.kvh; r.mb = it.mb; r.split = it.split;
-    r.q0 = it.q0; r.qn = it.qn; r.ctx = it.ctx; r.kv0 = it.kv0;
-    r.nnew = it.nnew; r.t0 = it.t0; r.n = it.n; r.flags = it.flags;
-    r.limit = it.limit; r.reserved = 0;
-    r.first_page = 0; r.n_pages = 0;
-#pragma unroll
-    for (int j = 0; j < kSchedPages; ++j) r.pages[j] = -1;
+    int first_page = 0, n_pages = 0;
+    const int32_t* bt = nullptr;
     if ((it.flags & SCHED_VALID) && a.max_blocks > 0 && it.ctx > 0) {
         const int last_key = min((it.t0 + it.n) * TILE_N, it.ctx) - 1;   // last cached key of the range
         if (last_key >= it.t0 * TILE_N) {
             const int last_page = min(last_key / a.page_size, a.max_blocks - 1);
-            r.first_page = max(0, last_page - (kSchedPages - 1));
-            r.n_pages = last_page - r.first_page + 1;
-            const int32_t* bt = a.block_tables + (int64_t)it.seq * a.bt_stride;
-            for (int j = 0; j < r.n_pages; ++j) r.pages[j] = bt[r.first_page + j];
+            first_page = max(0, last_page - (kSchedPages - 1));
+            n_pages = last_page - first_page + 1;
+            bt = a.block_tables + (int64_t)it.seq * a.bt_stride + first_page;
         }
     }
-    const uint4* src = reinterpret_cast<const uint4*>(&r);
-    uint4* dst = reinterpret_cast<uint4*>(out);
+    // four 16-byte stores of scalars, then the page ids four at a time (all loads of a group in flight together)
+    int4* dst = reinterpret_cast<int4*>(out);
+    dst[0] = make_int4(it.seq, it.kvh, it.mb, it.split);
+    dst[1] = make_int4(it.q0, it.qn, it.ctx, it.kv0);
+    dst[2] = make_int4(it.nnew, it.t0, it.n, it.flags);
+    dst[3] = make_int4(first_page, n_pages, it.limit, 0);
+    static_assert(offsetof(SchedRec, pages) == 64 && kSchedPages % 4 == 0, "record layout");
 #pragma unroll
-    for (int j = 0; j < (int)(sizeof(SchedRec) / 16); ++j) dst[j] = src[j];
+    for (int j = 0; j < kSchedPages; j += 4) {
+        int4 v;
+        v.x = j + 0 < n_pages ? bt[j + 0] : -1;
+        v.y = j + 1 < n_pages ? bt[j + 1] : -1;
+        v.z = j + 2 < n_pages ? bt[j + 2] : -1;
+        v.w = j + 3 < n_pages ? bt[j + 3] : -1;
+        dst[4 + j / 4] = v;
+    }
 }
 
 // cost of an item for the placement: its key tiles plus one tile's worth of per-item overhead
@@ -93,7 +98,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
     // bin << 16 | position inside the bin.
     __shared__ unsigned long long keys[SORT_MAX];
     __shared__ int offs[kSchedMaxBins + 1];
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, nthreads = blockDim.x;
     const int n_items = a.items_total, bins = a.bins;
     int32_t* off_out = const_cast<int32_t*>(a.sched_off);
     SchedRec* recs = const_cast<SchedRec*>(a.sched_recs);
@@ -101,7 +106,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
     if (n_items > SORT_MAX) {
         // Too many items to sort in shared memory: deal them round-robin in natural order (every item gets a
         // record, rows or not; kernels skip records without the VALID / EMPTY_SPLIT bits).
-        for (int b = tid; b <= bins; b += SCHED_THREADS) {
+        for (int b = tid; b <= bins; b += nthreads) {
             // bin b holds items b, b + bins, ...: offsets are the running counts
             int64_t before = 0;
             if (b > 0) {
@@ -110,7 +115,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
             }
             off_out[b] = (int)before;
         }
-        for (int i = tid; i < n_items; i += SCHED_THREADS) {
+        for (int i = tid; i < n_items; i += nthreads) {
             const int b = i % bins, pos = i / bins;
             const int full = n_items / bins, extra = n_items % bins;
             const int64_t base = (int64_t)full * b + min(b, extra);
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
 
     int n_pad = 1;
     while (n_pad < n_items) n_pad <<= 1;
-    for (int i = tid; i < n_pad; i += SCHED_THREADS) {
+    for (int i = tid; i < n_pad; i += nthreads) {
         unsigned long long key = ~0ull;
         if (i < n_items) {
             const uint32_t c = item_cost(item_shape(a, i));
@@ -133,7 +138,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
     // bitonic sort, ascending
     for (int k = 2; k <= n_pad; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = tid; i < n_pad; i += SCHED_THREADS) {
+            for (int i = tid; i < n_pad; i += nthreads) {
                 const int ixj = i ^ j;
                 if (ixj > i) {
                     const unsigned long long x = keys[i], y = keys[ixj];
@@ -148,51 +153,52 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
     // words (load << 8 | bin), so that one warp-wide minimum per item finds the least loaded bin, lowest index on ties;
     // that bin's lane takes the item.  The first `bins` items meet empty bins: item i goes to bin i, with no search.
     if (tid < 32) {
-        constexpr int PER_LANE = kSchedMaxBins / 32;
+        static_assert(kSchedMaxBins == 160, "five bins per lane, written out below");
         static_assert(kSchedMaxBins <= 256, "bin index is packed into 8 bits");
-        uint32_t load[PER_LANE], count[PER_LANE];
-        int i0 = 0;
-#pragma unroll
-        for (int j = 0; j < PER_LANE; ++j) {
+        // bins lane, lane + 32, ..., lane + 128 in five scalars each (indexed arrays would live in local memory)
+        uint32_t l0, l1, l2, l3, l4, c0 = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0;
+        auto first = [&](int j, uint32_t& l, uint32_t& cnt) {
             const int b = lane + 32 * j;
-            load[j] = 0xffffffffu; count[j] = 0;
+            l = 0xffffffffu;
             if (b < bins) {
                 uint32_t c = 0;
                 if (b < n_items) {
                     const unsigned long long key = keys[b];
                     c = 0xffffffffu - (uint32_t)(key >> 32);
-                    if (c != 0) { keys[b] = ((unsigned long long)((uint32_t)b << 16) << 32) | (uint32_t)key; count[j] = 1; }
+                    if (c != 0) { keys[b] = ((unsigned long long)((uint32_t)b << 16) << 32) | (uint32_t)key; cnt = 1; }
                 }
-                load[j] = (c << 8) | (uint32_t)b;
+                l = (c << 8) | (uint32_t)b;
             }
-        }
+        };
+        first(0, l0, c0); first(1, l1, c1); first(2, l2, c2); first(3, l3, c3); first(4, l4, c4);
         __syncwarp();
-        i0 = min(bins, n_items);
+        const int i0 = min(bins, n_items);
         unsigned long long key = i0 < n_items ? keys[i0] : ~0ull;
         for (int i = i0; i < n_items; ++i) {
             const unsigned long long cur = key;
             if (i + 1 < n_items) key = keys[i + 1];   // next item's key, off the critical path
             const uint32_t c = 0xffffffffu - (uint32_t)(cur >> 32);
             if (c == 0) break;   // the rest have no rows
-            uint32_t best = load[0];
-#pragma unroll
-            for (int j = 1; j < PER_LANE; ++j) best = min(best, load[j]);
+            const uint32_t best = min(min(min(l0, l1), min(l2, l3)), l4);
             const uint32_t win = __reduce_min_sync(0xffffffffu, best);
-            const uint32_t wb = win & 0xffu;
-            if ((wb & 31u) == (uint32_t)lane) {
-#pragma unroll
-                for (int j = 0; j < PER_LANE; ++j)
-                    if (j == (int)(wb >> 5)) {
-                        keys[i] = ((unsigned long long)((wb << 16) | count[j]) << 32) | (uint32_t)cur;
-                        load[j] += c << 8; count[j] += 1;
-                    }
-            }
+            const uint32_t wb = win & 0xffu, sel = wb >> 5;
+            const bool mine = (wb & 31u) == (uint32_t)lane;
+            const uint32_t inc = mine ? c << 8 : 0u, one = mine ? 1u : 0u;
+            const uint32_t pos = sel == 0 ? c0 : sel == 1 ? c1 : sel == 2 ? c2 : sel == 3 ? c3 : c4;
+            if (mine) keys[i] = ((unsigned long long)((wb << 16) | pos) << 32) | (uint32_t)cur;
+            l0 += sel == 0 ? inc : 0u; c0 += sel == 0 ? one : 0u;
+            l1 += sel == 1 ? inc : 0u; c1 += sel == 1 ? one : 0u;
+            l2 += sel == 2 ? inc : 0u; c2 += sel == 2 ? one : 0u;
+            l3 += sel == 3 ? inc : 0u; c3 += sel == 3 ? one : 0u;
+            l4 += sel == 4 ? inc : 0u; c4 += sel == 4 ? one : 0u;
         }
-        // offsets = exclusive prefix of the counts, in bin order (bin b = lane + 32 j)
         __syncwarp();
-#pragma unroll
-        for (int j = 0; j < PER_LANE; ++j)
-            if (lane + 32 * j < bins) offs[lane + 32 * j + 1] = (int)count[j];
+        if (lane < bins) offs[lane + 1] = (int)c0;
+        if (lane + 32 < bins) offs[lane + 33] = (int)c1;
+        if (lane + 64 < bins) offs[lane + 65] = (int)c2;
+        if (lane + 96 < bins) offs[lane + 97] = (int)c3;
+        if (lane + 128 < bins) offs[lane + 129] = (int)c4;
+        // offsets = exclusive prefix of the counts, in bin order
         __syncwarp();
         if (lane == 0) {
             offs[0] = 0;
@@ -201,9 +207,9 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
         __syncwarp();
     }
     __syncthreads();
-    for (int b = tid; b <= bins; b += SCHED_THREADS) off_out[b] = offs[b];
+    for (int b = tid; b <= bins; b += nthreads) off_out[b] = offs[b];
     const int placed = offs[bins];
-    for (int i = tid; i < placed; i += SCHED_THREADS) {
+    for (int i = tid; i < placed; i += nthreads) {
         const int item = (int)(uint32_t)keys[i];
         const uint32_t pl = (uint32_t)(keys[i] >> 32);
         write_record(a, item_shape(a, item), recs + offs[pl >> 16] + (pl & 0xffffu));
@@ -242,7 +248,10 @@ void tc5_plan_items(DecodeArgs& a, bool two_ctas, int sm_count) {
 int launch_decode_sched(const DecodeArgs& a, cudaStream_t st) {
     if (a.sched_off == nullptr || a.sched_recs == nullptr) return fail(DLX_ERR_WORKSPACE, "decode schedule: no buffer");
     if (a.bins < 1 || a.bins > kSchedMaxBins) return fail(DLX_ERR_INVALID_ARGUMENT, "decode schedule: %d bins", a.bins);
-    decode_sched_kernel<<<1, SCHED_THREADS, 0, st>>>(a);
+    // one block; as many threads as items (a power of two, 128..1024): fewer warps make the sort's barriers cheaper
+    int threads = 128;
+    while (threads < SCHED_THREADS && threads < a.items_total) threads <<= 1;
+    decode_sched_kernel<<<1, threads, 0, st>>>(a);
     return check_launch("decode_sched_kernel");
 }
 

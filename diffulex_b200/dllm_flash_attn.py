@@ -60,17 +60,30 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     args = (md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv, float(scale), max_q, max_kv, _MASKS[mask_name],
             dbs, num_splits)
     sched = _schedule(md, q, k, k_cache, v_cache, args)
-    if out is None:
-        o = ops.decode_attn(q, k, v, k_cache, v_cache, *args, sched)
-    else:
-        ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, sched)
-        o = out
+    o = _run(out, q, k, v, k_cache, v_cache, args, sched)
     if getattr(md, "check_status", False):
         bits, site, tile, cta = ops.device_status()
         if bits & 1:
             raise RuntimeError(f"decode attention: a bounded wait gave up (site {site}, tile {tile}, CTA {cta}); "
                                "the output of this call is incomplete")
     return o
+
+
+def _run(out, q, k, v, k_cache, v_cache, args, sched):
+    """One launch.  Under torch.compile the registered custom operators are used (they carry the fake
+    implementations a tracer needs); eager calls go straight to the C ABI: the dispatcher costs more host time than
+    the rest of the call."""
+    if torch.compiler.is_compiling():
+        if out is None:
+            return ops.decode_attn(q, k, v, k_cache, v_cache, *args, sched)
+        ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, sched)
+        return out
+    if out is None:
+        out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), device=q.device, dtype=q.dtype)
+    elif out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must have q's shape and dtype")
+    ops._decode_launch(q, k, v, k_cache, v_cache, out, *args, sched)
+    return out
 
 
 _ENV_NUM_SPLITS = int(os.environ.get("DLX_NUM_SPLITS", "0"))
@@ -133,7 +146,4 @@ def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
     args = (no_tables, no_context, md.cu_seqlens_q, md.cu_seqlens_k, float(scale), max_q, max_kv, mask, dbs,
             int(getattr(md, "num_splits", 0) or 1))
     sched = _schedule(md, q, k, no_cache, no_cache, args)
-    if out is None:
-        return ops.decode_attn(q, k, v, no_cache, no_cache, *args, sched)
-    ops.decode_attn_out(out, q, k, v, no_cache, no_cache, *args, sched)
-    return out
+    return _run(out, q, k, v, no_cache, no_cache, args, sched)

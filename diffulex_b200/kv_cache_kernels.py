@@ -25,7 +25,10 @@ def store_kvcache_unified_layout(key: torch.Tensor, value: torch.Tensor, k_cache
     assert k_cache.stride(1) == D and v_cache.stride(1) == D
     assert N == slot_mapping.numel(), f"`N`: {N}, `slot_mapping.numel()`: {slot_mapping.numel()}"
     assert value.shape == key.shape and k_cache.dtype == key.dtype and v_cache.dtype == value.dtype
-    ops.store_kvcache_unified(key, value, k_cache, v_cache, slot_mapping)
+    if torch.compiler.is_compiling():   # the registered operator carries what a tracer needs
+        ops.store_kvcache_unified(key, value, k_cache, v_cache, slot_mapping)
+    else:                               # eager: straight to the C ABI, the dispatcher costs more than the call
+        ops._store_unified_launch(key, value, k_cache, v_cache, slot_mapping)
 
 
 def store_kvcache_distinct_layout(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,

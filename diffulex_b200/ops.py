@@ -20,7 +20,13 @@ from ._lib import DecodeAttnParams, DlxError, check
 _DTYPES = {torch.bfloat16: _lib.DLX_DTYPE_BF16}
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream() -> int:
+    """The current CUDA stream of the current device as an integer handle."""
+    if _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device())
     return torch.cuda.current_stream().cuda_stream
 
 
@@ -31,9 +37,7 @@ def _need_cuda(*tensors: torch.Tensor) -> None:
 
 
 # ---- store -------------------------------------------------------------------------------------
-@torch.library.custom_op("dlx_b200::store_kvcache_unified", mutates_args=("k_cache", "v_cache"))
-def store_kvcache_unified(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                          slot_mapping: torch.Tensor) -> None:
+def _store_unified_launch(key, value, k_cache, v_cache, slot_mapping) -> None:
     _need_cuda(key, value, k_cache, v_cache, slot_mapping)
     n, heads, hd = key.shape
     d = heads * hd
@@ -46,6 +50,12 @@ def store_kvcache_unified(key: torch.Tensor, value: torch.Tensor, k_cache: torch
         key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
         slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), n, d, key.element_size(), num_slots,
         _stream()))
+
+
+@torch.library.custom_op("dlx_b200::store_kvcache_unified", mutates_args=("k_cache", "v_cache"))
+def store_kvcache_unified(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                          slot_mapping: torch.Tensor) -> None:
+    _store_unified_launch(key, value, k_cache, v_cache, slot_mapping)
 
 
 @torch.library.custom_op("dlx_b200::store_kvcache_distinct", mutates_args=("k_cache", "v_cache"))
@@ -223,6 +233,8 @@ def decode_schedule(q: torch.Tensor, k: torch.Tensor, k_cache: torch.Tensor, v_c
 
 def stream_capture_id() -> int:
     """Capture sequence id of the current stream (0 when it is not being captured)."""
+    if not torch.cuda.is_current_stream_capturing():
+        return 0
     cid = ctypes.c_uint64(0)
     check(_lib.lib().dlx_stream_capture_id(_stream(), ctypes.byref(cid)))
     return int(cid.value)
