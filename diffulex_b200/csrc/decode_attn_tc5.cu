@@ -3,18 +3,22 @@
 // Shape served: head_dim 128, bf16, any number G <= 128 of query heads per KV head.  All G heads of a KV head are
 // packed into the M dimension, so every K/V byte is read once per GROUP of heads.
 //
-// Work item = (sequence, KV head, block of 128 / G whole query tokens, key-range split).  The kernel is
-// persistent: one CTA per SM walks its share of the (longest-first) item list and keeps every ring and barrier
-// phase running across items, so the next item's Q/K/V land while the current one is finished.
+// Work item = (sequence, KV head, block of query tokens, key-range split); a CTA takes 128 / G whole tokens of it
+// (with more than 128 packed rows per KV head an item is two row blocks, run by the two neighbouring CTAs of a
+// schedule bin).  The kernel is persistent: a CTA walks the records the schedule kernel placed in its bin
+// (decode_sched.cu) and keeps every ring and barrier phase running across items, so the next item's Q/K/V land while
+// the current one is finished.  Prefill attention is the same kernel with an empty context.
 //
 // Warp roles (512 threads; after the split the warpgroups resize their register files with setmaxnreg):
 //   warps 0-7    two softmax warpgroups over the SAME 128 rows (thread <-> TMEM lane <-> query row), taking
-//                alternate key tiles: S -> registers, row max, P = exp2(s * scale - m_ref) as bf16 -> TMEM.
-//                m_ref is fixed by the item's first tile: no accumulator rescale ever runs
-//   warp 8, 9    K loader, V loader.  Tiles (128 keys) inside the cached prefix come by TMA
-//                (cp.async.bulk.tensor, 4-D map {hd, Hkv, page row, page}, 128-byte swizzle, plain per-CTA
-//                loads).  The tile with the end of the prefix: boxes of 64/32/16/8 rows for its cached rows, 16-byte
-//                cp.async for the < 8 left over and for the in-flight rows.  Page sizes that fit no box: cp.async
+//                alternate key tiles: S -> registers, P = exp2(s * scale - m_ref) as bf16 -> TMEM.  m_ref is the row
+//                maximum of the item's first tile: later tiles compute no maximum and no accumulator rescale ever
+//                runs.  An item whose exponents leave the safe range (tile row sum above 2^90, final row sum below
+//                2^-80) is marked and recomputed exactly before the CTA retires
+//   warp 8, 9    K loader, V loader: one lane each, everything by TMA.  Tiles (128 keys) inside the cached prefix:
+//                cp.async.bulk.tensor, 4-D map {hd, Hkv, page row, page}, 128-byte swizzle, plain per-CTA loads.
+//                The tile with the end of the prefix and the in-flight rows: boxes of 128 >> level rows from
+//                per-level maps, starting at any row of the tile
 //   warp 10      one thread issues S = Q K^T (tcgen05.mma, SS form) and fetches Q (TMA, one box per head_dim half);
 //                the warp also allocates and frees TMEM
 //   warp 11      one thread issues O += P V (TS form: P from TMEM, V as MN-major B operand from the [key][hd] tile)

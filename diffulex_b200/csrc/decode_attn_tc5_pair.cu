@@ -8,7 +8,8 @@
 // 128 head_dim columns for O += P V -- with ordinary per-CTA TMA boxes; the tensor cores read the other half from the
 // peer's shared memory.  Against two independent CTAs on the same item this halves the L2 -> SM traffic and the
 // shared-memory bytes written and read per tile, and the freed shared memory holds deeper K / V rings and a second
-// Q buffer.
+// Q buffer.  Measured, it is not faster than two independent CTAs (the hand-offs between the tensor pipe and the
+// softmax warps bound a tile, not the traffic), so it is taken on request only (kernel = 3).
 //
 // Work comes from a schedule built on the device once per metadata state (decode_sched.cu): records with every length
 // resolved and the first page ids attached, placed on the pairs by a longest-processing-time greedy.
@@ -26,7 +27,8 @@
 //   warps 12-15  epilogue warpgroup: O / l -> global through a swizzled staging buffer
 // Barriers that the issuing threads wait on live in the even CTA and count arrivals of both CTAs (one elected lane per
 // warp); barriers that announce MMA completion are signalled in both CTAs by one multicast tcgen05.commit.
-// TMEM (512 columns per CTA): S[2] (128 fp32 columns each) | P[2] (64 columns each) | O (128).
+// TMEM (512 columns per CTA): three score buffers of 128 fp32 columns, P (bf16) written over the first 64 columns of
+// its own score buffer once the scores are in registers | O (128).
 //
 // Every wait is bounded; on expiry the CTA raises an abort word, everyone drains, the place goes to a device status
 // word, both CTAs meet at a cluster barrier, TMEM is freed and the CTA returns (no trap).
