@@ -59,8 +59,7 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     num_splits = int(getattr(md, "num_splits", 0) or _ENV_NUM_SPLITS)
     args = (md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv, float(scale), max_q, max_kv, _MASKS[mask_name],
             dbs, num_splits)
-    sched = _schedule(md, q, k, k_cache, v_cache, args)
-    o = _run(out, q, k, v, k_cache, v_cache, args, sched)
+    o = _run(out, q, k, v, k_cache, v_cache, args, _plan(md, q, k, v, k_cache, v_cache, args))
     if getattr(md, "check_status", False):
         bits, site, tile, cta = ops.device_status()
         if bits & 1:
@@ -69,51 +68,50 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     return o
 
 
-def _run(out, q, k, v, k_cache, v_cache, args, sched):
+def _run(out, q, k, v, k_cache, v_cache, args, plan):
     """One launch.  Under torch.compile the registered custom operators are used (they carry the fake
-    implementations a tracer needs); eager calls go straight to the C ABI: the dispatcher costs more host time than
-    the rest of the call."""
+    implementations a tracer needs); eager calls go straight to the C ABI with the step's prepared parameter block:
+    the dispatcher and the parameter marshalling cost more host time than the rest of the call."""
     if torch.compiler.is_compiling():
         if out is None:
-            return ops.decode_attn(q, k, v, k_cache, v_cache, *args, sched)
-        ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, sched)
+            return ops.decode_attn(q, k, v, k_cache, v_cache, *args, plan.schedule)
+        ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, plan.schedule)
         return out
     if out is None:
         out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), device=q.device, dtype=q.dtype)
-    elif out.shape != q.shape or out.dtype != q.dtype:
-        raise ValueError("out must have q's shape and dtype")
-    ops._decode_launch(q, k, v, k_cache, v_cache, out, *args, sched)
+    ops.decode_launch_planned(plan, q, k, v, k_cache, v_cache, out)
     return out
 
 
 _ENV_NUM_SPLITS = int(os.environ.get("DLX_NUM_SPLITS", "0"))
-_captured_schedules = []   # schedules made inside a stream capture: the graph reads them on every replay
+_captured_plans = []   # plans made inside a stream capture: the graph reads their schedules on every replay
 
 
-def _schedule(md, q, k, k_cache, v_cache, args) -> "torch.Tensor | None":
-    """The step's schedule (``ops.decode_schedule``): built by the first layer call that sees a metadata
-    state and shared by the others through a memo on the metadata object.  The memo is keyed on the
+def _plan(md, q, k, v, k_cache, v_cache, args) -> "ops.DecodePlan":
+    """The step's plan (``ops.decode_plan``: schedule + prepared parameter block): built by the first layer call that
+    sees a metadata state and shared by the others through a memo on the metadata object.  The memo is keyed on the
     metadata tensors (storage and in-place version), the shapes that shape the plan, and the capture id of
     the current stream: inside a CUDA-graph capture the first layer call always records a planning launch,
     so a replay after the runner refilled its static buffers (diffulex/strategy/block_diffusion/engine/
     model_runner.py:183-195) plans from the new lengths."""
     block_tables, context_lens, cu_q, cu_kv = args[0], args[1], args[2], args[3]
     cap = ops.stream_capture_id()
-    key = (cap, ops.DECODE_KERNEL, q.shape[0], q.shape[1], k.shape[1], k_cache.shape[1], args[5:],
-           tuple((t.data_ptr(), t._version, t.numel()) if t is not None else None
-                 for t in (block_tables, context_lens, cu_q, cu_kv)))
-    memo = getattr(md, "_dlx_schedule", None)
+    key = (cap, ops.DECODE_KERNEL, q.shape, k.shape, k_cache.shape, args[4:],
+           block_tables.data_ptr(), block_tables._version, block_tables.shape, block_tables.stride(0),
+           context_lens.data_ptr(), context_lens._version, cu_q.data_ptr(), cu_q._version, cu_q.shape,
+           None if cu_kv is None else (cu_kv.data_ptr(), cu_kv._version))
+    memo = getattr(md, "_dlx_plan", None)
     if memo is not None and memo[0] == key:
         return memo[1]
-    sched = ops.decode_schedule(q, k, k_cache, v_cache, *args)
+    plan = ops.decode_plan(q, k, v, k_cache, v_cache, *args)
     try:
-        md._dlx_schedule = (key, sched)
+        md._dlx_plan = (key, plan)
     except AttributeError:
         pass
-    if cap and sched is not None:
-        _captured_schedules.append(sched)
-        del _captured_schedules[:-64]
-    return sched
+    if cap and plan.schedule is not None:
+        _captured_plans.append(plan)
+        del _captured_plans[:-64]
+    return plan
 
 
 def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
@@ -145,5 +143,4 @@ def dllm_flash_attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
     mask = DLX_MASK_BLOCK_CAUSAL if kind == "block_attention" else DLX_MASK_FULL
     args = (no_tables, no_context, md.cu_seqlens_q, md.cu_seqlens_k, float(scale), max_q, max_kv, mask, dbs,
             int(getattr(md, "num_splits", 0) or 1))
-    sched = _schedule(md, q, k, no_cache, no_cache, args)
-    return _run(out, q, k, v, no_cache, no_cache, args, sched)
+    return _run(out, q, k, v, no_cache, no_cache, args, _plan(md, q, k, v, no_cache, no_cache, args))

@@ -177,6 +177,56 @@ def _decode_launch(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
     check(handle.dlx_decode_attn(ctypes.byref(p), _stream()))
 
 
+class DecodePlan:
+    """What every layer call of one step shares: the schedule buffer, the parameter block with everything but the
+    per-layer tensors filled in, and the scratch the call needs besides the schedule."""
+    __slots__ = ("schedule", "template", "workspace_bytes", "q_shape", "kv_shape", "cache_shape")
+
+
+def decode_plan(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits) -> DecodePlan:
+    """Validates once, launches the planning kernel (``decode_schedule``) and keeps the filled parameter block, so
+    that the layer calls of the step (``decode_launch_planned``) only patch their own tensors in."""
+    sched = decode_schedule(q, k, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                            max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
+    p = _decode_params(q, k, v, k_cache, v_cache, q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
+                       max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, sched)
+    handle = _lib.lib()
+    ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
+    if ws_bytes < 0:
+        check(int(-ws_bytes))
+    if sched is not None:
+        ws_bytes -= handle.dlx_decode_attn_schedule_bytes(ctypes.byref(p))
+    plan = DecodePlan()
+    plan.schedule, plan.template, plan.workspace_bytes = sched, bytes(p), int(ws_bytes)
+    plan.q_shape, plan.kv_shape, plan.cache_shape = q.shape, k.shape, k_cache.shape
+    return plan
+
+
+def decode_launch_planned(plan: DecodePlan, q, k, v, k_cache, v_cache, out) -> None:
+    """One layer's launch over a step's plan: same shapes as the tensors the plan was made with, any pointers and
+    row / page strides."""
+    hd = q.shape[2]
+    if q.shape != plan.q_shape or k.shape != plan.kv_shape or v.shape != plan.kv_shape or out.shape != plan.q_shape \
+            or k_cache.shape != plan.cache_shape or v_cache.shape != plan.cache_shape:
+        raise ValueError("tensor shapes differ from the ones this step was planned for")
+    for t in (q, k, v, out):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or t.stride(2) != 1 or t.stride(1) != hd:
+            raise ValueError("q / k / v / out: CUDA bf16 [tokens, heads, head_dim] with contiguous heads")
+    p = DecodeAttnParams.from_buffer_copy(plan.template)
+    p.q, p.k, p.v, p.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    p.q_row_stride, p.k_row_stride, p.v_row_stride, p.out_row_stride = q.stride(0), k.stride(0), v.stride(0), out.stride(0)
+    if k_cache.numel() > 0:
+        if not k_cache.is_cuda or k_cache.stride() != v_cache.stride() or k_cache.stride(3) != 1 or k_cache.stride(2) != hd:
+            raise ValueError("cache must be CUDA [pages, page_size, Hkv, head_dim] with contiguous heads, K and V alike")
+        p.k_cache, p.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+        p.cache_page_stride, p.cache_token_stride = k_cache.stride(0), k_cache.stride(1)
+    if plan.workspace_bytes > 0:
+        ws = torch.empty(plan.workspace_bytes, device=q.device, dtype=torch.uint8)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), plan.workspace_bytes
+    check(_lib.lib().dlx_decode_attn(ctypes.byref(p), _stream()))
+
+
 @torch.library.custom_op("dlx_b200::decode_attn", mutates_args=())
 def decode_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
@@ -259,4 +309,4 @@ def planned_num_splits(q, k, v, k_cache, v_cache, block_tables, context_lens, cu
 
 
 __all__ = ["store_kvcache_unified", "store_kvcache_distinct", "load_kvcache", "decode_attn", "decode_attn_out",
-           "decode_schedule", "stream_capture_id", "device_status", "planned_num_splits", "DlxError"]
+           "decode_schedule", "decode_plan", "decode_launch_planned", "DecodePlan", "stream_capture_id", "device_status", "planned_num_splits", "DlxError"]
