@@ -51,6 +51,8 @@ _SIGNATURES = {
                                           c_int64, c_int64, c_int, c_int64, c_void_p]),
     "dlx_store_kvcache_distinct": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                                            c_int64, c_int32, c_int32, c_int32, c_int32, c_int64, c_int, c_void_p]),
+    "dlx_build_slot_mapping": (c_int, [c_void_p, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                       c_int64, c_int64, c_void_p, c_int, c_void_p]),
     "dlx_load_kvcache": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                  c_void_p, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_int64, c_int32, c_int32, c_int64, c_int64, c_int, c_void_p]),

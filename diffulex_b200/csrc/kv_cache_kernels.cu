@@ -353,3 +353,65 @@ extern "C" int dlx_load_kvcache(const void* k_cache, const void* v_cache, int64_
 #undef DLX_LOAD_ARGS
     return check_launch("load_kvcache_kernel");
 }
+
+// ---- slot mapping of a decode step, built on the device ----------------------------------------
+// Row t of the step's in-flight K / V belongs to sequence s (cu_seqlens_q[s] <= t < cu_seqlens_q[s + 1]) and sits at
+// position ctx_s + (t - cu_seqlens_q[s]) of it; its cache slot is page_table[s][pos / PAGE] * PAGE + pos % PAGE.
+// Sequences whose block is still being denoised store nothing (-1), as do positions without a page.
+namespace dlx {
+__global__ void __launch_bounds__(256) build_slot_mapping_kernel(
+    const int32_t* __restrict__ block_tables, int64_t bt_stride, int max_blocks, const int32_t* __restrict__ context_lens,
+    const int32_t* __restrict__ cu_q, const int32_t* __restrict__ store_flags, int num_seqs, int page_size,
+    int64_t total_rows, int32_t* __restrict__ slots32, int64_t* __restrict__ slots64) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total_rows; t += (int64_t)gridDim.x * blockDim.x) {
+        // The sequence that owns row t: binary search over the offsets.  A captured step's static buffers are
+        // zero-filled behind the live sequences (model_runner.py:183-186), so the offsets are not monotone there: when
+        // the search ends on a sequence that does not hold t, every sequence is tried in turn.
+        int lo = 0, hi = num_seqs;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if ((int64_t)cu_q[mid] <= t) lo = mid; else hi = mid;
+        }
+        int64_t q0 = cu_q[lo], q1 = cu_q[lo + 1];
+        if (!(t >= q0 && t < q1)) {
+            for (int s = 0; s < num_seqs; ++s) {
+                const int64_t a0 = cu_q[s], a1 = cu_q[s + 1];
+                if (t >= a0 && t < a1) { lo = s; q0 = a0; q1 = a1; break; }
+            }
+        }
+        int64_t slot = -1;
+        if (t >= q0 && t < q1 && (store_flags == nullptr || store_flags[lo] != 0)) {
+            const int64_t pos = (int64_t)max(context_lens[lo], 0) + (t - q0);
+            const int64_t j = pos / page_size;
+            if (j < max_blocks) {
+                const int32_t pid = block_tables[(int64_t)lo * bt_stride + j];
+                if (pid >= 0) slot = (int64_t)pid * page_size + (pos - j * page_size);
+            }
+        }
+        if (slots32 != nullptr) slots32[t] = (int32_t)slot; else slots64[t] = slot;
+    }
+}
+}  // namespace dlx
+
+extern "C" int dlx_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride, int32_t max_blocks,
+                                      const int32_t* context_lens, const int32_t* cu_seqlens_q,
+                                      const int32_t* store_flags, int32_t num_seqs, int32_t page_size,
+                                      int64_t total_rows, int64_t num_pages, void* slot_mapping, int slots_are_int64,
+                                      void* stream) {
+    using namespace dlx;
+    if (num_seqs < 0 || total_rows < 0 || page_size <= 0 || max_blocks < 0 || num_pages < 0)
+        return fail(DLX_ERR_INVALID_ARGUMENT, "slot mapping: negative or zero size");
+    if (total_rows == 0) return DLX_OK;
+    if (!slot_mapping || !cu_seqlens_q || !context_lens || (max_blocks > 0 && !block_tables))
+        return fail(DLX_ERR_INVALID_ARGUMENT, "slot mapping: null pointer");
+    if (num_seqs == 0) return fail(DLX_ERR_INVALID_ARGUMENT, "slot mapping: rows without sequences");
+    if (!slots_are_int64 && num_pages * (int64_t)page_size > 0x7fffffffll)
+        return fail(DLX_ERR_UNSUPPORTED, "slot mapping: %lld slots do not fit int32", (long long)(num_pages * page_size));
+    int64_t ctas = (total_rows + 255) / 256;
+    if (ctas > (int64_t)kNumSMs * 8) ctas = (int64_t)kNumSMs * 8;
+    build_slot_mapping_kernel<<<(unsigned)ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        block_tables, block_table_stride, max_blocks, context_lens, cu_seqlens_q, store_flags, num_seqs, page_size,
+        total_rows, slots_are_int64 ? nullptr : static_cast<int32_t*>(slot_mapping),
+        slots_are_int64 ? static_cast<int64_t*>(slot_mapping) : nullptr);
+    return check_launch("build_slot_mapping_kernel");
+}

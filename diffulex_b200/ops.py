@@ -71,6 +71,33 @@ def store_kvcache_distinct(key: torch.Tensor, value: torch.Tensor, k_cache: torc
         key.element_size(), _stream()))
 
 
+def build_slot_mapping(block_tables: torch.Tensor, context_lens: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                       page_size: int, total_rows: int, num_pages: int, store_flags: Optional[torch.Tensor] = None,
+                       out: Optional[torch.Tensor] = None, dtype: torch.dtype = torch.int32) -> torch.Tensor:
+    """The decode step's ``slot_mapping`` computed on the device from the page tables (C ABI:
+    dlx_build_slot_mapping; the reference builds it in a host loop and copies it over every step,
+    diffulex/strategy/block_diffusion/engine/model_runner.py:141-156).  ``store_flags[s] == 0``: sequence s stores
+    nothing this step (-1 for its rows).  Writes ``out`` (a static buffer of a captured step) when given.  No host
+    sync; capturable."""
+    _need_cuda(block_tables, context_lens, cu_seqlens_q, store_flags, out)
+    for name, t in (("block_tables", block_tables), ("context_lens", context_lens), ("cu_seqlens_q", cu_seqlens_q),
+                    ("store_flags", store_flags)):
+        if t is not None and (t.dtype != torch.int32 or (t.dim() == 1 and not t.is_contiguous())):
+            raise ValueError(f"{name} must be contiguous int32")
+    if block_tables.dim() != 2 or (block_tables.shape[1] > 0 and block_tables.stride(1) != 1):
+        raise ValueError("block_tables must be [num_seqs, max_blocks] with contiguous rows")
+    if out is None:
+        out = torch.empty(total_rows, dtype=dtype, device=block_tables.device)
+    if out.dtype not in (torch.int32, torch.int64) or out.numel() < total_rows or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 or int64 tensor of at least total_rows entries")
+    check(_lib.lib().dlx_build_slot_mapping(
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(),
+        cu_seqlens_q.data_ptr(), store_flags.data_ptr() if store_flags is not None else None,
+        cu_seqlens_q.numel() - 1, page_size, total_rows, num_pages, out.data_ptr(), int(out.dtype == torch.int64),
+        _stream()))
+    return out
+
+
 # ---- load --------------------------------------------------------------------------------------
 @torch.library.custom_op("dlx_b200::load_kvcache", mutates_args=())
 def load_kvcache(k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
@@ -308,5 +335,5 @@ def planned_num_splits(q, k, v, k_cache, v_cache, block_tables, context_lens, cu
     return n
 
 
-__all__ = ["store_kvcache_unified", "store_kvcache_distinct", "load_kvcache", "decode_attn", "decode_attn_out",
+__all__ = ["store_kvcache_unified", "store_kvcache_distinct", "build_slot_mapping", "load_kvcache", "decode_attn", "decode_attn_out",
            "decode_schedule", "decode_plan", "decode_launch_planned", "DecodePlan", "stream_capture_id", "device_status", "planned_num_splits", "DlxError"]

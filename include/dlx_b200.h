@@ -94,6 +94,22 @@ int dlx_load_kvcache(const void* k_cache, const void* v_cache, int64_t cache_pag
                      int32_t page_size, int64_t num_pages, int64_t row_elems, int elem_bytes, void* stream);
 
 /*
+ * The slot mapping of a decode step, built on the device: what the reference's model runner builds in a Python
+ * loop and copies over every step (diffulex/strategy/block_diffusion/engine/model_runner.py:118, 141-151, 156).
+ * Row t of the step's in-flight K/V belongs to the sequence s with cu_seqlens_q[s] <= t < cu_seqlens_q[s+1] and is
+ * position pos = context_lens[s] + (t - cu_seqlens_q[s]) of it:
+ *     slot[t] = block_tables[s][pos / page_size] * page_size + pos % page_size
+ * and -1 (store nothing) when store_flags[s] == 0 (the sequence's block is still being denoised, :141-142), when the
+ * position has no page (table entry -1 or pos / page_size >= max_blocks), or when t belongs to no sequence
+ * (padding).  store_flags == NULL: every sequence stores.  For page sizes that divide the diffusion block this is
+ * the reference's list of whole pages (:143-151).  slot_mapping: int32 or int64, total_rows entries.
+ */
+int dlx_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride, int32_t max_blocks,
+                           const int32_t* context_lens, const int32_t* cu_seqlens_q, const int32_t* store_flags,
+                           int32_t num_seqs, int32_t page_size, int64_t total_rows, int64_t num_pages,
+                           void* slot_mapping, int slots_are_int64, void* stream);
+
+/*
  * Paged block-diffusion decode attention.  For sequence s, query rows
  * q[cu_seqlens_q[s] .. cu_seqlens_q[s+1]) of every query head attend to
  * [cached keys 0..context_lens[s]-1 (through block_tables) ; in-flight keys k/v[kv0 .. kv0+new)]

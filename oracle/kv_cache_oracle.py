@@ -113,3 +113,39 @@ def reference_written_rows(page, block_tables, context_lens, seq_lens, cu_seqlen
         nfull = (new // dbs) * dbs
         m[o + ctx:o + ctx + nfull] = True
     return m
+
+
+def build_slot_mapping(block_tables, context_lens, cu_seqlens_q, page_size, total_rows, store_flags=None) -> np.ndarray:
+    """Slot of every in-flight row of a decode step: position ``ctx + i`` of its sequence through the page table,
+    -1 for sequences that store nothing this step, for positions without a page and for rows of no sequence.
+    The reference's runner writes ``[-1] * block`` for a sequence whose block is still active and otherwise the
+    whole slot ranges of the block's pages (diffulex/strategy/block_diffusion/engine/model_runner.py:141-151);
+    ``reference_bd_slot_mapping`` below restates that loop, and for page sizes that divide the diffusion block the
+    two agree (tests/test_oracle_golden.py)."""
+    out = np.full(total_rows, -1, dtype=np.int64)
+    maxb = block_tables.shape[1]
+    for s in range(len(context_lens)):
+        q0, q1 = int(cu_seqlens_q[s]), int(cu_seqlens_q[s + 1])
+        if q1 <= q0 or (store_flags is not None and not store_flags[s]):
+            continue
+        for t in range(max(q0, 0), min(q1, total_rows)):
+            pos = max(int(context_lens[s]), 0) + (t - q0)
+            j = pos // page_size
+            if j < maxb and block_tables[s, j] >= 0:
+                out[t] = int(block_tables[s, j]) * page_size + pos % page_size
+    return out
+
+
+def reference_bd_slot_mapping(block_table_lists, to_cache, diffusion_block_size, page_size) -> list:
+    """The reference runner's own loop (model_runner.py:141-151): per sequence ``[-1] * dbs`` while its last block
+    is active, else the slot ranges of the last ``dbs // page_size`` pages of its table."""
+    slots = []
+    for table, store in zip(block_table_lists, to_cache):
+        if not store:
+            slots.extend([-1] * diffusion_block_size)
+            continue
+        n_pages = diffusion_block_size // page_size
+        for i in range(n_pages):
+            start = table[len(table) - n_pages + i] * page_size
+            slots.extend(range(start, start + page_size))
+    return slots

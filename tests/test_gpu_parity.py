@@ -97,6 +97,37 @@ def test_store_distinct_layout_bit_exact(name, dlx, golden_dir):
     assert digest(kcd.cpu()) == golden["k_cache"] and digest(vcd.cpu()) == golden["v_cache"]
 
 
+# ---- slot mapping built on the device ----------------------------------------------------------
+@pytest.mark.parametrize("name", ["cfg1", "ragged_q", "ragged_permuted", "q4_gqa4"])
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+def test_slot_mapping_built_on_the_device_bit_exact(name, dtype, dlx):
+    """Against the oracle: every sequence storing, some sequences still denoising (-1 rows), a zero-filled padded
+    tail as a replayed graph's static buffers have it, and rows behind the last sequence."""
+    from diffulex_b200 import ops
+    p = attn_problem(ATTN_CASES[name])
+    pd = to_dev(p)
+    g = p.geometry
+    rows, nb = p.q.shape[0], p.k_cache.shape[0]
+    got = ops.build_slot_mapping(pd.block_tables, pd.context_lens, pd.cu_seqlens_q, g.page_size, rows, nb, dtype=dtype)
+    want = kv_cache_oracle.build_slot_mapping(p.block_tables.numpy(), p.context_lens.numpy(), p.cu_seqlens_q.numpy(),
+                                              g.page_size, rows)
+    assert got.dtype == dtype and np.array_equal(got.cpu().numpy().astype(np.int64), want)
+    assert np.array_equal(want, p.slot_mapping.numpy().astype(np.int64))
+    flags = torch.tensor([s % 2 for s in range(p.num_seqs)], dtype=torch.int32)
+    pad = 5
+    z = lambda t, n: torch.cat([t, torch.zeros(n, dtype=t.dtype)])
+    cu_q, ctx = z(p.cu_seqlens_q, pad), z(p.context_lens, pad)
+    bt = torch.cat([p.block_tables, torch.zeros(pad, p.block_tables.shape[1], dtype=torch.int32)])
+    fl = z(flags, pad)
+    out = torch.full((rows + 7,), 12345, dtype=dtype, device="cuda")
+    ret = ops.build_slot_mapping(bt.cuda(), ctx.cuda(), cu_q.cuda(), g.page_size, rows + 7, nb, store_flags=fl.cuda(),
+                                 out=out)
+    assert ret is out
+    want = kv_cache_oracle.build_slot_mapping(bt.numpy(), ctx.numpy(), cu_q.numpy(), g.page_size, rows + 7, fl.numpy())
+    assert (want[rows:] == -1).all()
+    assert np.array_equal(out.cpu().numpy().astype(np.int64), want)
+
+
 # ---- load --------------------------------------------------------------------------------------
 @pytest.mark.parametrize("name", list(LOAD_CASES))
 def test_load_bit_exact(name, dlx, golden_dir):

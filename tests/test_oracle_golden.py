@@ -106,3 +106,31 @@ def test_prefill_oracle_matches_reference(name, golden_dir):
     o = attn_oracle.prefill_attention(q, k, v, cu_q, cu_k, case["hd"] ** -0.5, case["block"], case["dbs"])
     rows, heads = prefill_fixture_index(case)
     torch.testing.assert_close(o[rows][:, heads], want, atol=2e-5, rtol=1e-5)
+
+
+def test_slot_mapping_oracle_restates_the_runner_loop_and_the_workload_generator():
+    """Positions through the page table == the reference runner's whole-page lists when pages divide the block
+    (diffulex/strategy/block_diffusion/engine/model_runner.py:141-151), == the slots the seeded workloads carry."""
+    from diffulex_b200.workload import make_problem, small_workload
+    rng = np.random.default_rng(7)
+    dbs, page = 32, 16
+    # block-aligned contexts, tables that end with the pages of the in-flight block
+    ctx = np.array([64, 0, 160, 32]); to_cache = [True, False, True, True]
+    tables, nb = [], 0
+    for c in ctx:
+        n = (c + dbs) // page
+        tables.append(list(rng.permutation(200)[:n] + 0)); nb = max(nb, n)
+    bt = np.full((len(ctx), nb), -1, dtype=np.int32)
+    for s, t in enumerate(tables):
+        bt[s, :len(t)] = t
+    cu_q = np.arange(0, (len(ctx) + 1) * dbs, dbs, dtype=np.int32)
+    got = kv_cache_oracle.build_slot_mapping(bt, ctx.astype(np.int32), cu_q, page, int(cu_q[-1]),
+                                             np.array(to_cache, dtype=np.int32))
+    want = kv_cache_oracle.reference_bd_slot_mapping(tables, to_cache, dbs, page)
+    assert got.tolist() == want
+    # the seeded workloads' slot mappings (ragged contexts, 64- and 256-row pages, permuted tables)
+    for name in ("ragged_q", "cfg1", "q4_gqa4"):
+        p = attn_problem(ATTN_CASES[name])
+        got = kv_cache_oracle.build_slot_mapping(p.block_tables.numpy(), p.context_lens.numpy(), p.cu_seqlens_q.numpy(),
+                                                 p.geometry.page_size, p.q.shape[0])
+        assert np.array_equal(got, p.slot_mapping.numpy().astype(np.int64))
