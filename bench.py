@@ -652,7 +652,7 @@ def main():
             cur = torch.cuda.current_stream()
             s_in.wait_stream(cur)
             m = SimpleNamespace(**vars(md))
-            m.__dict__.pop("_dlx_schedule", None)      # a new step: the schedule is planned again from the copied metadata
+            m.__dict__.pop("_dlx_plan", None)          # a new step: the schedule is planned again from the copied metadata
             with torch.cuda.stream(s_in):
                 if copies:
                     for n_, t in h_meta.items():

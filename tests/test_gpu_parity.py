@@ -494,7 +494,7 @@ def test_captured_step_replans_when_the_metadata_buffers_are_refilled(dlx):
     torch.testing.assert_close(o1.float().cpu(), want, atol=ATOL, rtol=RTOL)
     assert torch.equal(o1, o2)
     bins = 16   # 4 sequences x 4 KV heads: one item per CTA pair
-    off, recs = parse_schedule(md._dlx_schedule[1], bins)
+    off, recs = parse_schedule(md._dlx_plan[1].schedule, bins)
     recs = recs[: off[bins]]
     new_ctx = pb.host_context_lens
     assert all(r[6] == new_ctx[r[0]] for r in recs)
