@@ -325,31 +325,30 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 }
                 if (warp_valid) {
                     const int key0 = (it.t0 + tile_of(jj, n)) * TILE_N;
-                    float mx_any = -INFINITY;   // first tile only: row maximum over every real key, hidden ones included
-                    if (key0 + TILE_N > it.full_until) {
-                        // The tile touches a mask boundary (warp-uniform, one or two tiles per item): write -inf over
-                        // the hidden scores in TMEM first.  A small rolled loop on purpose: the common path below is
-                        // fully unrolled and should stay inside the instruction cache.
-#pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t wv[32];
-                            tmem_ld32(tS + c * 32, wv);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                if (jj == 0 && key0 + c * 32 + e < it.total) mx_any = fmaxf(mx_any, __uint_as_float(wv[e]));
-                                if (key0 + c * 32 + e >= limit) wv[e] = 0xff800000u;  // -inf
-                            }
-                            tmem_st32(tS + c * 32, wv);
-                        }
-                        tmem_st_wait();
-                    }
                     // the whole S row of this thread: 128 fp32 scores in registers, one TMEM round trip
                     uint32_t v[4][32];
                     tmem_ld32(tS, v[0]); tmem_ld32(tS + 32, v[1]); tmem_ld32(tS + 64, v[2]); tmem_ld32(tS + 96, v[3]);
                     tmem_ld_wait();
                     tc_fence_before();
                     mbar_arrive(bar(B_SFREE + w));   // S is in registers: the next Q K^T into this buffer may start now
+                    float mx_any = -INFINITY;   // first tile only: row maximum over every real key, hidden ones included
+                    if (key0 + TILE_N > it.full_until) {
+                        // The tile touches a mask boundary (warp-uniform; one or two tiles per item): hidden scores become
+                        // -inf in registers.  Only an item's first tile needs the maximum over its hidden keys as well.
+                        const int rel = limit - key0, rel_any = it.total - key0;
+                        if (jj == 0) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                                for (int e = 0; e < 32; ++e)
+                                    if (c * 32 + e < rel_any) mx_any = fmaxf(mx_any, __uint_as_float(v[c][e]));
+                        }
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                if (c * 32 + e >= rel) v[c][e] = 0xff800000u;
+                    }
                     if (jj == 0) {
                         // First tile: its row maximum fixes the reference (later tiles compute no maximum at all).  A row
                         // that sees none of this tile's keys (block-causal rows of an early block; the first tile is a
