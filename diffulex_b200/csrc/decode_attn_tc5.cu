@@ -768,8 +768,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 ok = mbar_wait(bar(B_VFULL + idx % VSTAGES), (idx / VSTAGES) & 1, abort_flag, 8, k);
                 ok = ok && mbar_wait(bar(B_PFULL + b), u & 1, abort_flag, 9, k);
                 if (!ok) break;
-                fence_async_proxy();
-                tc_fence_after();
+                tc_fence_after();   // V arrived by TMA (async proxy): no proxy fence is needed before the MMA reads it
                 const uint32_t vb = sV + (idx % VSTAGES) * ITEM_BYTES;
                 const uint32_t pa = tmem + TM_P + b * 64;
                 const uint64_t dv = smem_desc(vb, REGION, 1024);
