@@ -82,9 +82,9 @@ constexpr int NUM_THREADS = 512;
 // Registers per thread after the roles split (the kernel starts with 65536 / 512 = 128 each): the four helper warps
 // and the epilogue warpgroup give registers back, the two softmax warpgroups (a row of 128 scores each) take them.
 #ifndef DLX_SOFTMAX_REGS
-#define DLX_SOFTMAX_REGS 184
+#define DLX_SOFTMAX_REGS 176
 #define DLX_HELPER_REGS 56
-#define DLX_EPI_REGS 88
+#define DLX_EPI_REGS 104
 #endif
 constexpr int SOFTMAX_REGS = DLX_SOFTMAX_REGS, HELPER_REGS = DLX_HELPER_REGS, EPI_REGS = DLX_EPI_REGS;
 static_assert(2 * SOFTMAX_REGS + HELPER_REGS + EPI_REGS <= 512, "register budget");
@@ -508,7 +508,10 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                     // bf16 output, 64 head_dim columns (128 bytes of each row) per pass.  A thread holds one ROW, so direct
                     // stores would touch 32 different lines per instruction; the pass goes through a swizzled staging
                     // buffer instead and leaves as 4 rows x 128 contiguous bytes per instruction.
-#pragma unroll 1
+                    // Both halves are pulled out of TMEM before anything is written (the first one waits as 32 packed
+                    // registers): the next item's first P V is held up by O_free, not by the stores.
+                    uint32_t pk[2][32];
+#pragma unroll
                     for (int c = 0; c < 2; ++c) {
                         uint32_t v[2][32];
                         tmem_ld32(tO + c * 64, v[0]);
@@ -519,13 +522,16 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                             mbar_arrive(bar(B_OFREE));   // O is in registers: the next item's P V may overwrite it
                         }
 #pragma unroll
+                        for (int e = 0; e < 64; e += 2)
+                            pk[c][e >> 1] = pack2<__nv_bfloat16>(__uint_as_float(v[e >> 5][e & 31]) * inv, __uint_as_float(v[e >> 5][(e & 31) + 1]) * inv);
+                    }
+#pragma unroll 1
+                    for (int c = 0; c < 2; ++c) {
+#pragma unroll
                         for (int q4 = 0; q4 < 8; ++q4) {
-                            const uint32_t* x = &v[q4 >> 2][(q4 & 3) * 8];
                             uint4 o;
-                            o.x = pack2<__nv_bfloat16>(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv);
-                            o.y = pack2<__nv_bfloat16>(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv);
-                            o.z = pack2<__nv_bfloat16>(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv);
-                            o.w = pack2<__nv_bfloat16>(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv);
+                            if (c == 0) o = make_uint4(pk[0][q4 * 4], pk[0][q4 * 4 + 1], pk[0][q4 * 4 + 2], pk[0][q4 * 4 + 3]);
+                            else o = make_uint4(pk[1][q4 * 4], pk[1][q4 * 4 + 1], pk[1][q4 * 4 + 2], pk[1][q4 * 4 + 3]);
                             *reinterpret_cast<uint4*>(stage + lane * 128 + ((q4 ^ (lane & 7)) << 4)) = o;
                         }
                         __syncwarp();
