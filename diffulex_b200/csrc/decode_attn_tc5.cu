@@ -182,6 +182,13 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     extern __shared__ unsigned char smem_raw[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+    // This CTA's records: placed by the schedule kernel (longest-processing-time greedy, longest item first).  Two
+    // neighbouring CTAs walk the same list when an item is two row blocks: they run side by side, and the second
+    // reader of a K / V tile finds it in L2.  The offsets are asked for first: their trip to memory overlaps the set-up.
+    const int bin = (int)blockIdx.x / a_param.group_ctas, rank = (int)blockIdx.x - bin * a_param.group_ctas;
+    const int rec0 = a_param.sched_off[bin];
+    const int n_rounds = a_param.sched_off[bin + 1] - rec0;
+
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     unsigned char* gbase = smem_raw + (sbase - smem_u32(smem_raw));
     const uint32_t sQ = sbase, sK = sbase + OFF_K, sV = sbase + OFF_V, sBar = sbase + OFF_BAR;
@@ -199,39 +206,21 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
     const DecodeArgs& a = *reinterpret_cast<const DecodeArgs*>(gbase + OFF_ARGS);   // for use AFTER the set-up barrier
     const int G = a_param.group;
 
-    if (tid == 0) {
-        mbar_init(bar(B_QFULL), 1);
-        mbar_init(bar(B_QEMPTY), 1);
-        for (int s = 0; s < KSTAGES; ++s) { mbar_init(bar(B_KFULL + s), 1); mbar_init(bar(B_KEMPTY + s), 1); }
-        for (int s = 0; s < VSTAGES; ++s) { mbar_init(bar(B_VFULL + s), 1); mbar_init(bar(B_VEMPTY + s), 1); }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(B_SFULL + s), 1); mbar_init(bar(B_PFULL + s), 128);
-            mbar_init(bar(B_SFREE + s), 128); mbar_init(bar(B_PFREE + s), 1);
-        }
-        mbar_init(bar(B_OFULL), 1);
-        mbar_init(bar(B_OFREE), 128);
-        mbar_init(bar(B_EPIDONE), 128);
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(bar(B_MRFULL + s), 128); mbar_init(bar(B_MREMPTY + s), 128);
-            mbar_init(bar(B_LSFULL + s), 256); mbar_init(bar(B_LSEMPTY + s), 128);
-        }
-        *abort_flag = 0;
+    if (tid < B_COUNT) {   // one barrier per thread; expected arrivals by slot
+        uint32_t count = 1;
+        if (tid >= B_PFULL && tid < B_PFULL + 2) count = 128;
+        else if (tid >= B_SFREE && tid < B_SFREE + 2) count = 128;
+        else if (tid == B_OFREE || tid == B_EPIDONE) count = 128;
+        else if (tid >= B_MRFULL && tid < B_MRFULL + 2) count = 128;
+        else if (tid >= B_MREMPTY && tid < B_MREMPTY + 2) count = 128;
+        else if (tid >= B_LSFULL && tid < B_LSFULL + 2) count = 256;
+        else if (tid >= B_LSEMPTY && tid < B_LSEMPTY + 2) count = 128;
+        mbar_init(bar(tid), count);
+        if (tid == 0) *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    // This CTA's records: placed by the schedule kernel (longest-processing-time greedy, longest item first).
-    // (two neighbouring CTAs walk the same list when an item is two row blocks: they run side by side, and the second
-    // reader of a K / V tile finds it in L2)
-    const int bin = (int)blockIdx.x / a_param.group_ctas, rank = (int)blockIdx.x - bin * a_param.group_ctas;
-    const int rec0 = a_param.sched_off[bin];
-    const int n_rounds = a_param.sched_off[bin + 1] - rec0;
     const SchedRec* recs_g = a_param.sched_recs + rec0;
     SchedRec* recs_s = reinterpret_cast<SchedRec*>(gbase + OFF_ITEMS);
-    {
-        const int n_tab = min(n_rounds, MAX_ROUNDS);
-        const uint4* src = reinterpret_cast<const uint4*>(recs_g);
-        uint4* dst = reinterpret_cast<uint4*>(recs_s);
-        for (int i = tid; i < n_tab * (int)(sizeof(SchedRec) / 16); i += NUM_THREADS) dst[i] = src[i];
-    }
     auto rec_of = [&](int k) -> const SchedRec* { return k < MAX_ROUNDS ? recs_s + k : recs_g + k; };
     // Division by the (runtime) group size is slow; a block's rows always start at a whole token, so the split of a
     // row index into (token, head) is the same for every item and is tabulated once.
@@ -253,6 +242,12 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         for (int i = tid; i < (KSTAGES + VSTAGES) * ITEM_BYTES / 16; i += NUM_THREADS)
             *reinterpret_cast<uint4*>(gbase + OFF_K + i * 16) = make_uint4(0, 0, 0, 0);
         fence_async_proxy();
+    }
+    {   // the records, after everything that does not need them (the offsets have had time to arrive)
+        const int n_tab = min(n_rounds, MAX_ROUNDS);
+        const uint4* src = reinterpret_cast<const uint4*>(recs_g);
+        uint4* dst = reinterpret_cast<uint4*>(recs_s);
+        for (int i = tid; i < n_tab * (int)(sizeof(SchedRec) / 16); i += NUM_THREADS) dst[i] = src[i];
     }
     if (warp == QK_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(sBar + 8u * B_COUNT + 8u) : "memory");
