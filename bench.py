@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = the model's)")
     ap.add_argument("--num-splits", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-group", type=int, default=7, help="layers per host<->device copy group of the e2e step")
+    ap.add_argument("--e2e-group", type=int, default=2, help="layers per host<->device copy group of the e2e step")
     ap.add_argument("--no-strong", action="store_true", help="skip the cfg5 strong-scaling side measurement")
     ap.add_argument("--no-splitk", action="store_true", help="skip the split-K side measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
