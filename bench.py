@@ -46,7 +46,7 @@ import torch
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per decode launch of the workload, from an ncu capture of this
 # command on two resident layer caches; None where no capture has been taken.
-NCU_TRAFFIC_BYTES = {"cfg2": 178472448 + 7511296}
+NCU_TRAFFIC_BYTES = {"cfg2": 178475008 + 7841024}
 
 
 def parse():
