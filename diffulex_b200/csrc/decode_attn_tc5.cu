@@ -595,6 +595,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
         const uint32_t ring0 = which ? sV : sK;
         int stage = 0;            // ring position of the next tile
         uint32_t par_empty = 1;   // parity of "this slot is free" for the next tile (the first pass finds every slot free)
+        int issued = 0;           // tiles whose copies were issued (lane 0)
         bool alive = true;
 #pragma unroll 1
         for (int round = 0; round < n_rounds && alive; ++round) {
@@ -647,6 +648,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                             mbar_arrive_expect_tx(full, ITEM_BYTES);
                             tma_load_4d(d0, &cmaps[lvl0], 0, kvh, prow, pid0, full);
                             tma_load_4d(d0 + REGION, &cmaps[lvl0], 64, kvh, prow, pid0, full);
+                            ++issued;
                         }
                     } else {
                         // ---- the tile with the end of the prefix, in-flight rows, small pages ----
@@ -659,6 +661,7 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                         }
                         ok = mbar_wait(bar_empty0 + 8u * stage, par_empty, abort_flag, 5 + which, jj);
                         if (ok) {
+                            ++issued;
                             if (ce == 0) {
                                 mbar_arrive(full);
                             } else {
@@ -696,6 +699,17 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
             ++done; ck += n;
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing may still be landing when the CTA retires
+        if (lane == 0 && *abort_flag != 0) {
+            // A wait gave up somewhere in the CTA: boxes this lane has issued may still be in flight.  Each stage's
+            // "full" barrier completes when the bytes of its last copy have landed, whether or not anybody consumes
+            // them; wait for those phases (bounded) before the CTA hands its shared memory back.
+            for (int st = 0; st < stages; ++st) {
+                const int uses = (issued - st + stages - 1) / stages;   // tiles issued into stage st
+                if (uses < 1) continue;
+                for (uint32_t it = 0; it < (1u << 16); ++it)
+                    if (mbar_try(bar_full0 + 8u * st, (uint32_t)(uses - 1) & 1u)) break;
+            }
+        }
     } else if (warp == QK_WARP) {
       if (lane == 0) {
         // =========================== Q K^T issuer (one thread) ===========================
@@ -745,6 +759,11 @@ decode_attn_tc5_kernel(const DecodeArgs a_param, const __grid_constant__ TmaMaps
                 tc_commit(bar(B_KEMPTY + idx % KSTAGES));
             }
             if (ok) tc_commit(bar(B_QEMPTY));   // every Q K^T of this item has read Q
+            else {
+                // giving up with this item's Q copy possibly in flight: let it land first (bounded)
+                for (uint32_t it = 0; it < (1u << 16); ++it)
+                    if (mbar_try(bar(B_QFULL), done & 1)) break;
+            }
             ++done; ck += n;
         }
       }
