@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = the model's)")
     ap.add_argument("--num-splits", type=int, default=0)
+    ap.add_argument("--separate-store", action="store_true",
+                    help="one store launch and one attention launch per layer (default: the attention call stores too)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-group", type=int, default=2, help="layers per host<->device copy group of the e2e step")
     ap.add_argument("--no-strong", action="store_true", help="skip the cfg5 strong-scaling side measurement")
@@ -253,9 +255,9 @@ def strong_cfg5(dlx, dp, dev, rank, world, peak):
     md = p.metadata("static")
     out = torch.empty_like(p.q)
 
-    def step():
-        dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
-        dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md, out=out)
+    def step():   # one layer call: store the in-flight rows and attend
+        dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md, out=out,
+                                   store_slot_mapping=md.slot_mapping)
 
     for _ in range(3):
         step()
@@ -535,12 +537,20 @@ def main():
     splits = ops.planned_num_splits(base.q, base.k, base.v, base.k_cache, base.v_cache, base.block_tables,
                                     base.context_lens, base.cu_seqlens_q, base.cu_seqlens_k, base.scale,
                                     md.max_seqlen_q, 0, base.mask_mode, geo.diffusion_block_size, args.num_splits)
-    launches_per_layer = 2 + (1 if splits > 1 else 0)
+    fused = not args.separate_store   # the attention call also stores the layer's in-flight K / V rows
+    launches_per_layer = 2 + (1 if splits > 1 else 0)   # store kernel + attention kernel either way
+
+    def layer_call(q, k, v, p, m, out=None):
+        """What the attention layer does per decode call: store the in-flight rows, attend."""
+        if fused:
+            return dlx.dllm_flash_attn_decode(q, k, v, p.k_cache, p.v_cache, p.scale, m, out=out,
+                                              store_slot_mapping=m.slot_mapping)
+        dlx.store_kvcache_unified_layout(k, v, p.k_cache, p.v_cache, m.slot_mapping, m)
+        return dlx.dllm_flash_attn_decode(q, k, v, p.k_cache, p.v_cache, p.scale, m, out=out)
 
     def step(outs=None):
         for i, p in enumerate(layers):
-            dlx.store_kvcache_unified_layout(p.k, p.v, p.k_cache, p.v_cache, md.slot_mapping, md)
-            o = dlx.dllm_flash_attn_decode(p.q, p.k, p.v, p.k_cache, p.v_cache, p.scale, md)
+            o = layer_call(p.q, p.k, p.v, p, md)
             if outs is not None:
                 outs[i] = o
         return o
@@ -669,8 +679,7 @@ def main():
                 if kernels:
                     for i in g:
                         p = layers[i]
-                        dlx.store_kvcache_unified_layout(d_k[i], d_v[i], p.k_cache, p.v_cache, m.slot_mapping, m)
-                        dlx.dllm_flash_attn_decode(d_q[i], d_k[i], d_v[i], p.k_cache, p.v_cache, p.scale, m, out=d_out[i])
+                        layer_call(d_q[i], d_k[i], d_v[i], p, m, out=d_out[i])
                 ev_c[gi].record(cur)
                 s_out.wait_event(ev_c[gi])
                 if copies:
@@ -767,7 +776,8 @@ def main():
                        "heads": f"{geo.num_q_heads}q/{geo.num_kv_heads}kv x {geo.head_dim}", "page_size": geo.page_size,
                        "query_block": query_block, "kv_tokens_per_layer_per_gpu":
                        kv_tokens_layer, "num_splits": splits,
-                       "step": "L x (store_kvcache_unified + decode attention), CUDA-graph replay",
+                       "step": ("L x (one call: store kernel + decode attention kernel), CUDA-graph replay" if fused
+                                else "L x (store_kvcache_unified + decode attention), CUDA-graph replay"),
                        "l2": f"inputs larger than L2: {L} distinct layer caches, "
                              f"{kv_bytes_layer * L / 1e9:.2f} GB of KV per step",
                        "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.scaling})")},

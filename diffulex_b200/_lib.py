@@ -40,6 +40,7 @@ class DecodeAttnParams(ctypes.Structure):
         ("num_q_heads", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32), ("page_size", c_int32),
         ("max_q_len", c_int32), ("max_kv_len", c_int32), ("mask_mode", c_int32), ("diffusion_block_size", c_int32),
         ("num_splits", c_int32), ("kernel", c_int32), ("scale", c_float), ("total_kv", c_int32),
+        ("slot_mapping", c_void_p), ("slots_are_int64", c_int32), ("reserved0", c_int32),
     ]
 
 

@@ -3,7 +3,7 @@ the one caller of the three operators on the decode hot path.  Per layer call it
 
 1. views the projections ``[s, heads * hd]`` as ``[s, heads, hd]`` (:45-47),
 2. writes the step's K / V rows into the paged cache when the metadata asks for it and a cache is attached
-   (:53-57; unified or split layout by ``kv_cache_layout``),
+   (:53-57; unified or split layout by ``kv_cache_layout``); in decode this is part of the attention call,
 3. runs prefill or decode attention (:60-69) and
 4. returns ``[s, heads * hd]`` contiguous (:72).
 
@@ -40,13 +40,16 @@ class Attention(torch.nn.Module):
         md = self.fetch_attn_metadata()
         unified = getattr(md, "kv_cache_layout", "unified") == "unified"
         have_cache = self.k_cache.numel() > 0 and self.v_cache.numel() > 0
-        if have_cache and getattr(md, "need_kv_cache_store", True):
+        store_now = have_cache and getattr(md, "need_kv_cache_store", True)
+        fused = store_now and unified and not md.is_prefill   # decode: the attention call stores as well
+        if store_now and not fused:
             store = store_kvcache_unified_layout if unified else store_kvcache_distinct_layout
             store(k, v, self.k_cache, self.v_cache, md.slot_mapping, md)
         if md.is_prefill:
             o = dllm_flash_attn_prefill(q, k, v, self.scale, md)
         elif unified:
-            o = dllm_flash_attn_decode(q, k, v, self.k_cache, self.v_cache, self.scale, md)
+            o = dllm_flash_attn_decode(q, k, v, self.k_cache, self.v_cache, self.scale, md,
+                                       store_slot_mapping=md.slot_mapping if fused else None)
         else:
             # as in the reference (attn_impl.py:68-69): decode reads the unified layout only
             raise NotImplementedError("decode attention reads the unified cache layout only")

@@ -261,6 +261,16 @@ extern "C" int dlx_decode_attn(const dlx_decode_attn_params* p, void* stream) {
         a.ws_lse = static_cast<float*>(p->workspace);
         a.ws_o = reinterpret_cast<float*>(static_cast<char*>(p->workspace) + d.ws_lse_bytes);
     }
+    if (p->slot_mapping != nullptr && p->max_blocks > 0) {
+        // The call also stores: the store kernel runs first, on the same stream.  (Storing from inside the attention
+        // kernel was measured slower than this 3 us launch: it held up the epilogue warps of the items that did it.)
+        if (p->cache_token_stride != (int64_t)p->num_kv_heads * hd || p->cache_page_stride != p->cache_token_stride * p->page_size)
+            return fail(DLX_ERR_UNSUPPORTED, "decode with store: the flat-slot store kernel needs contiguous cache pages");
+        rc = dlx_store_kvcache_unified(p->k, p->k_row_stride, p->v, p->v_row_stride, const_cast<void*>(p->k_cache),
+                                       const_cast<void*>(p->v_cache), p->slot_mapping, p->slots_are_int64, a.total_kv,
+                                       (int64_t)p->num_kv_heads * hd, 2, p->num_pages * (int64_t)p->page_size, stream);
+        if (rc != DLX_OK) return rc;
+    }
     if (d.use_tc5) {
         if (own_schedule) {
             // no prepared schedule: plan this launch now, into the tail of the workspace

@@ -32,10 +32,16 @@ _MASKS = {None: DLX_MASK_FULL, "bd_full": DLX_MASK_FULL, "varlen_full": DLX_MASK
 
 
 def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
-                           v_cache: torch.Tensor, scale: float, attn_metadata, out: "torch.Tensor | None" = None
-                           ) -> torch.Tensor:
+                           v_cache: torch.Tensor, scale: float, attn_metadata, out: "torch.Tensor | None" = None,
+                           store_slot_mapping: "torch.Tensor | None" = None) -> torch.Tensor:
     """``q [sumQ, Hq, hd]``, ``k/v [sumQ, Hkv, hd]``, unified caches ``[NB, PAGE, Hkv, hd]`` ->
     new tensor ``o [sumQ, Hq, hd]`` in q's dtype (or ``out``, additive keyword, when given).
+
+    ``store_slot_mapping`` (additive keyword): when given, the call also stores the in-flight ``k`` / ``v`` rows
+    into the caches at these flat slots, i.e. it does ``store_kvcache_unified_layout`` and the attention of
+    ``Attention.forward`` (diffulex/attention/attn_impl.py:54-57, :66-67) in one call (the store kernel is launched
+    first, on the same stream; one trip through Python and the C ABI instead of two); the caller then skips its own
+    store.
 
     Optional metadata attributes (all additive): ``mask_mode``, ``num_splits``, and ``check_status``:
     when true the call synchronises afterwards, reads the kernels' status word and raises if a bounded
@@ -59,7 +65,8 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     num_splits = int(getattr(md, "num_splits", 0) or _ENV_NUM_SPLITS)
     args = (md.block_tables, md.context_lens, md.cu_seqlens_q, cu_kv, float(scale), max_q, max_kv, _MASKS[mask_name],
             dbs, num_splits)
-    o = _run(out, q, k, v, k_cache, v_cache, args, _plan(md, q, k, v, k_cache, v_cache, args))
+    o = _run(out, q, k, v, k_cache, v_cache, args, _plan(md, q, k, v, k_cache, v_cache, args, store_slot_mapping),
+             store_slot_mapping)
     if getattr(md, "check_status", False):
         bits, site, tile, cta = ops.device_status()
         if bits & 1:
@@ -68,11 +75,13 @@ def dllm_flash_attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_
     return o
 
 
-def _run(out, q, k, v, k_cache, v_cache, args, plan):
+def _run(out, q, k, v, k_cache, v_cache, args, plan, slots=None):
     """One launch.  Under torch.compile the registered custom operators are used (they carry the fake
     implementations a tracer needs); eager calls go straight to the C ABI with the step's prepared parameter block:
     the dispatcher and the parameter marshalling cost more host time than the rest of the call."""
     if torch.compiler.is_compiling():
+        if slots is not None:   # the traced operators do not store: a separate store operator first
+            ops.store_kvcache_unified(k, v, k_cache, v_cache, slots)
         if out is None:
             return ops.decode_attn(q, k, v, k_cache, v_cache, *args, plan.schedule)
         ops.decode_attn_out(out, q, k, v, k_cache, v_cache, *args, plan.schedule)
@@ -87,7 +96,7 @@ _ENV_NUM_SPLITS = int(os.environ.get("DLX_NUM_SPLITS", "0"))
 _captured_plans = []   # plans made inside a stream capture: the graph reads their schedules on every replay
 
 
-def _plan(md, q, k, v, k_cache, v_cache, args) -> "ops.DecodePlan":
+def _plan(md, q, k, v, k_cache, v_cache, args, slots=None) -> "ops.DecodePlan":
     """The step's plan (``ops.decode_plan``: schedule + prepared parameter block): built by the first layer call that
     sees a metadata state and shared by the others through a memo on the metadata object.  The memo is keyed on the
     metadata tensors (storage and in-place version), the shapes that shape the plan, and the capture id of
@@ -99,11 +108,12 @@ def _plan(md, q, k, v, k_cache, v_cache, args) -> "ops.DecodePlan":
     key = (cap, ops.DECODE_KERNEL, q.shape, k.shape, k_cache.shape, args[4:],
            block_tables.data_ptr(), block_tables._version, block_tables.shape, block_tables.stride(0),
            context_lens.data_ptr(), context_lens._version, cu_q.data_ptr(), cu_q._version, cu_q.shape,
-           None if cu_kv is None else (cu_kv.data_ptr(), cu_kv._version))
+           None if cu_kv is None else (cu_kv.data_ptr(), cu_kv._version),
+           None if slots is None else (slots.data_ptr(), slots.dtype))
     memo = getattr(md, "_dlx_plan", None)
     if memo is not None and memo[0] == key:
         return memo[1]
-    plan = ops.decode_plan(q, k, v, k_cache, v_cache, *args)
+    plan = ops.decode_plan(q, k, v, k_cache, v_cache, *args, slots)
     try:
         md._dlx_plan = (key, plan)
     except AttributeError:

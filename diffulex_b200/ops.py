@@ -133,7 +133,7 @@ DECODE_KERNEL = int(os.environ.get("DLX_DECODE_KERNEL", "0"))
 
 def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv,
                    scale, max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits,
-                   schedule=None) -> DecodeAttnParams:
+                   schedule=None, slot_mapping=None) -> DecodeAttnParams:
     if q.dtype not in _DTYPES:
         raise ValueError(f"decode attention is built for bf16, got {q.dtype}")
     total_q, hq, hd = q.shape
@@ -166,6 +166,11 @@ def _decode_params(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
         p.schedule, p.schedule_bytes = schedule.data_ptr(), schedule.numel() * schedule.element_size()
     p.total_q, p.num_seqs = total_q, cu_seqlens_q.numel() - 1
     p.total_kv = k.shape[0]
+    if slot_mapping is not None:   # the call also stores the in-flight rows
+        if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous() \
+                or slot_mapping.numel() != k.shape[0]:
+            raise ValueError("slot_mapping must be a contiguous int32 or int64 tensor with one entry per row of k")
+        p.slot_mapping, p.slots_are_int64 = slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64)
     p.num_q_heads, p.num_kv_heads, p.head_dim = hq, hkv, hd
     p.max_q_len, p.max_kv_len = max_q_len, max_kv_len
     p.mask_mode, p.diffusion_block_size = mask_mode, diffusion_block_size
@@ -207,17 +212,20 @@ def _decode_launch(q, k, v, k_cache, v_cache, out, block_tables, context_lens, c
 class DecodePlan:
     """What every layer call of one step shares: the schedule buffer, the parameter block with everything but the
     per-layer tensors filled in, and the scratch the call needs besides the schedule."""
-    __slots__ = ("schedule", "template", "workspace_bytes", "q_shape", "kv_shape", "cache_shape")
+    __slots__ = ("schedule", "template", "workspace_bytes", "q_shape", "kv_shape", "cache_shape", "slot_mapping")
 
 
 def decode_plan(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
-                max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits) -> DecodePlan:
+                max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, slot_mapping=None) -> DecodePlan:
     """Validates once, launches the planning kernel (``decode_schedule``) and keeps the filled parameter block, so
-    that the layer calls of the step (``decode_launch_planned``) only patch their own tensors in."""
+    that the layer calls of the step (``decode_launch_planned``) only patch their own tensors in.  With
+    ``slot_mapping`` every layer call of the step also stores its in-flight K / V rows (C ABI: the ``slot_mapping``
+    field of the parameter block)."""
+    _need_cuda(slot_mapping)
     sched = decode_schedule(q, k, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
                             max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits)
     p = _decode_params(q, k, v, k_cache, v_cache, q, block_tables, context_lens, cu_seqlens_q, cu_seqlens_kv, scale,
-                       max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, sched)
+                       max_q_len, max_kv_len, mask_mode, diffusion_block_size, num_splits, sched, slot_mapping)
     handle = _lib.lib()
     ws_bytes = handle.dlx_decode_attn_workspace_bytes(ctypes.byref(p))
     if ws_bytes < 0:
@@ -227,6 +235,7 @@ def decode_plan(q, k, v, k_cache, v_cache, block_tables, context_lens, cu_seqlen
     plan = DecodePlan()
     plan.schedule, plan.template, plan.workspace_bytes = sched, bytes(p), int(ws_bytes)
     plan.q_shape, plan.kv_shape, plan.cache_shape = q.shape, k.shape, k_cache.shape
+    plan.slot_mapping = slot_mapping   # kept alive: the parameter block points at it
     return plan
 
 

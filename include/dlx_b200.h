@@ -165,6 +165,13 @@ typedef struct dlx_decode_attn_params {
     float scale;                 /* softmax scale, hd^-1/2 in every shipped model                      */
     int32_t total_kv;            /* rows of k / v; 0 = total_q.  Bounds the tcgen05 kernels' copies of
                                     in-flight rows: rows past it read as zero                           */
+    const void* slot_mapping;    /* optional, [rows of k / v] int32 or int64: the call ALSO stores the in-flight
+                                    K / V rows into the caches at these flat slots (negative = skip), i.e. it does
+                                    the work of dlx_store_kvcache_unified + dlx_decode_attn (attn_impl.py:54-57 and
+                                    :66-67) in one call: the store kernel is launched first on the same stream
+                                    (needs contiguous cache pages).  NULL: attention only                       */
+    int32_t slots_are_int64;
+    int32_t reserved0;
 } dlx_decode_attn_params;
 
 /* Bytes of scratch dlx_decode_attn needs for these parameters when it plans itself (split-K partials

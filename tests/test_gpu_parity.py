@@ -501,6 +501,38 @@ def test_captured_step_replans_when_the_metadata_buffers_are_refilled(dlx):
     assert [int(r[0]) for r in recs[:4]] == [1, 1, 1, 1], "the longest sequence of the NEW step comes first"
 
 
+# ---- decode that also stores -------------------------------------------------------------------
+@pytest.mark.parametrize("kernel", ["auto", "tc5", "pair", "mma"])
+@pytest.mark.parametrize("num_splits", [0, 3])
+@pytest.mark.parametrize("name", ["cfg1", "ragged_q", "ragged_permuted", "q4_gqa4", "ref_head_dim_64", "d2f_gqa7"])
+def test_decode_that_also_stores_equals_store_then_decode(name, num_splits, kernel, dlx, monkeypatch):
+    """``store_slot_mapping``: one call does the layer's store and its attention.  Caches bit-exact against the
+    store oracle (some rows skipped through negative slots, int32 and int64 slots), output against the attention
+    oracle; on every kernel (the ones that do not store by themselves run the store kernel first)."""
+    from diffulex_b200 import ops
+    case = ATTN_CASES.get(name) or D2F_CASES[name]
+    p = attn_problem(case)
+    if kernel in ("tc5", "pair") and p.geometry.head_dim != 128:
+        pytest.skip("the tcgen05 kernels serve head_dim 128")
+    monkeypatch.setattr(ops, "DECODE_KERNEL", KERNELS[kernel])
+    want = oracle_out(p)
+    for slot_dtype, drop in ((torch.int32, 0), (torch.int64, 3)):
+        slots = p.slot_mapping.clone().to(slot_dtype)
+        if drop:
+            slots[::drop] = -1
+        kc_ref, vc_ref = bits(p.k_cache).copy(), bits(p.v_cache).copy()
+        kv_cache_oracle.store_kvcache_unified(bits(p.k), bits(p.v), kc_ref, vc_ref, slots.numpy())
+        pd = to_dev(p)
+        md = pd.metadata("static")
+        md.num_splits = num_splits
+        o = dlx.dllm_flash_attn_decode(pd.q, pd.k, pd.v, pd.k_cache, pd.v_cache, pd.scale, md,
+                                       store_slot_mapping=slots.cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(pd.k_cache), kc_ref) and np.array_equal(bits(pd.v_cache), vc_ref)
+        torch.testing.assert_close(o.float().cpu(), want, atol=ATOL, rtol=RTOL)
+    assert ops.device_status()[0] == 0
+
+
 # ---- error behaviour ---------------------------------------------------------------------------
 def test_errors_are_raised_before_launch(dlx):
     p = attn_problem(ATTN_CASES["ragged_q"])
