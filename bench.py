@@ -155,7 +155,7 @@ def cpu_attention_baseline(w, budget_s=12.0):
         t = time.time(); attn_oracle.decode_attention(*args); times.append(time.time() - t)
     dt = statistics.median(times)
     return (p.kv_bytes() / dt / 1e9, int(p.host_new_lens.sum()) / dt, cores,
-            f"1 of {w.geometry.layers} layers, all {p.num_seqs} sequences, fp32, {len(times)} runs, median")
+            f"1 of {w.geometry.layers} layers, all {p.num_seqs} sequences, fp32, {len(times)} runs, median", dt * 1e3)
 
 
 def store_load_bandwidth(dlx, dev, peak, num_seqs=256):
@@ -472,10 +472,10 @@ def run_reference(args, w, rank, world):
     vals = []
     for _ in range(args.warmup):
         pass  # warm-up happens inside cpu_attention_baseline
-    gbs, toks, cores, sample = cpu_attention_baseline(w, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
+    gbs, toks, cores, sample, sample_ms = cpu_attention_baseline(w, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
     line = {
         "impl": "reference", "metric": "decode_attn_kv_read_gbps", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sample_ms, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "query_tokens_per_s": toks,
         "config": {"workload": f"{w.name}: {w.note}", "sample": sample},
@@ -759,7 +759,7 @@ def main():
         torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, toks, cores, sample = cpu_attention_baseline(w_global)
+        gbs, toks, cores, sample, _ = cpu_attention_baseline(w_global)
         cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample,
                "query_tokens_per_s": toks}
     if sampler:
