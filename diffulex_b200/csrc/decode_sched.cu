@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
     // bin << 16 | position inside the bin.
     __shared__ unsigned long long keys[SORT_MAX];
     __shared__ int offs[kSchedMaxBins + 1];
+    __shared__ int n_live_s;   // items with rows
     const int tid = threadIdx.x, lane = tid & 31, nthreads = blockDim.x;
     const int n_items = a.items_total, bins = a.bins;
     int32_t* off_out = const_cast<int32_t*>(a.sched_off);
@@ -126,14 +127,20 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
 
     int n_pad = 1;
     while (n_pad < n_items) n_pad <<= 1;
+    if (tid == 0) n_live_s = 0;
+    __syncthreads();
+    int live_here = 0;
     for (int i = tid; i < n_pad; i += nthreads) {
         unsigned long long key = ~0ull;
         if (i < n_items) {
             const uint32_t c = item_cost(item_shape(a, i));
             key = ((unsigned long long)(0xffffffffu - c) << 32) | (uint32_t)i;
+            live_here += c != 0;
         }
         keys[i] = key;
     }
+    live_here = __reduce_add_sync(0xffffffffu, live_here);
+    if (lane == 0 && live_here) atomicAdd(&n_live_s, live_here);
     __syncthreads();
     // bitonic sort, ascending
     for (int k = 2; k <= n_pad; k <<= 1) {
@@ -150,8 +157,8 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
         }
     }
     // Longest-processing-time greedy by one warp: every lane keeps the loads of bins lane, lane + 32, ... as packed
-    // words (load << 8 | bin), so that one warp-wide minimum per item finds the least loaded bin, lowest index on ties;
-    // that bin's lane takes the item.  The first `bins` items meet empty bins: item i goes to bin i, with no search.
+    // words (load << 8 | bin), so that one warp minimum finds the least loaded bin, lowest index on ties; that bin's
+    // lane takes the item.  The first `bins` items meet empty bins: item i goes to bin i, with no search.
     if (tid < 32) {
         static_assert(kSchedMaxBins == 160, "five bins per lane, written out below");
         static_assert(kSchedMaxBins <= 256, "bin index is packed into 8 bits");
@@ -172,25 +179,48 @@ __global__ void __launch_bounds__(SCHED_THREADS) decode_sched_kernel(const Decod
         };
         first(0, l0, c0); first(1, l1, c1); first(2, l2, c2); first(3, l3, c3); first(4, l4, c4);
         __syncwarp();
-        const int i0 = min(bins, n_items);
-        unsigned long long key = i0 < n_items ? keys[i0] : ~0ull;
-        for (int i = i0; i < n_items; ++i) {
-            const unsigned long long cur = key;
-            if (i + 1 < n_items) key = keys[i + 1];   // next item's key, off the critical path
-            const uint32_t c = 0xffffffffu - (uint32_t)(cur >> 32);
-            if (c == 0) break;   // the rest have no rows
-            const uint32_t best = min(min(min(l0, l1), min(l2, l3)), l4);
-            const uint32_t win = __reduce_min_sync(0xffffffffu, best);
-            const uint32_t wb = win & 0xffu, sel = wb >> 5;
-            const bool mine = (wb & 31u) == (uint32_t)lane;
-            const uint32_t inc = mine ? c << 8 : 0u, one = mine ? 1u : 0u;
-            const uint32_t pos = sel == 0 ? c0 : sel == 1 ? c1 : sel == 2 ? c2 : sel == 3 ? c3 : c4;
-            if (mine) keys[i] = ((unsigned long long)((wb << 16) | pos) << 32) | (uint32_t)cur;
-            l0 += sel == 0 ? inc : 0u; c0 += sel == 0 ? one : 0u;
-            l1 += sel == 1 ? inc : 0u; c1 += sel == 1 ? one : 0u;
-            l2 += sel == 2 ? inc : 0u; c2 += sel == 2 ? one : 0u;
-            l3 += sel == 3 ? inc : 0u; c3 += sel == 3 ? one : 0u;
-            l4 += sel == 4 ? inc : 0u; c4 += sel == 4 ? one : 0u;
+        // The rest of the items, several independent greedy placements side by side: bins and lanes fall into `nsets`
+        // sets by index modulo nsets (a lane's bins lane, lane + 32, ... all lie in set lane % nsets), and the sorted
+        // item i belongs to set (i % bins) % nsets, so that every run of `bins` consecutive items gives each set as
+        // many items as it has bins.  A few butterfly exchanges per step give every set its minimum: a step places
+        // nsets items (warp exchanges are what a step costs; within 1 % of one global placement for sets of ten
+        // bins).  With few bins one set holds them all: the plain greedy placement.
+        const int nsets = bins >= 32 ? 8 : bins >= 16 ? 4 : 1;
+        const int s4 = lane & (nsets - 1);
+        const int n_live = n_live_s;               // the first n_live sorted items have rows
+        const int blocks = (n_live + bins - 1) / bins - 1;              // runs of `bins` items after the first
+        const int max_steps = blocks > 0 ? blocks * ((bins + nsets - 1) / nsets) : 0;
+        int blk = 1, pp = s4;                      // the set's next item is blk * bins + pp
+        unsigned long long key = ~0ull;
+        if (s4 < bins && bins + pp < n_live) key = keys[bins + pp];
+        for (int step = 0; step < max_steps; ++step) {
+            const int i = blk * bins + pp;
+            const bool active = s4 < bins && i < n_live;
+            // the set's least loaded bin (all lanes take part in the exchanges, sets that are done included)
+            uint32_t win = min(min(min(l0, l1), min(l2, l3)), l4);
+            if (nsets == 1) {
+                win = __reduce_min_sync(0xffffffffu, win);
+            } else {
+                for (int off = nsets; off < 32; off <<= 1) win = min(win, __shfl_xor_sync(0xffffffffu, win, off));
+            }
+            if (active) {
+                const unsigned long long cur = key;
+                const uint32_t c = 0xffffffffu - (uint32_t)(cur >> 32);
+                int p2 = pp + nsets, blk2 = blk;
+                if (p2 >= bins) { p2 = s4; ++blk2; }
+                if (blk2 * bins + p2 < n_live) key = keys[blk2 * bins + p2];   // next item's key, off the critical path
+                const uint32_t wb = win & 0xffu, sel = wb >> 5;
+                const bool mine = (wb & 31u) == (uint32_t)lane;
+                const uint32_t inc = mine ? c << 8 : 0u, one = mine ? 1u : 0u;
+                const uint32_t pos = sel == 0 ? c0 : sel == 1 ? c1 : sel == 2 ? c2 : sel == 3 ? c3 : c4;
+                if (mine) keys[i] = ((unsigned long long)((wb << 16) | pos) << 32) | (uint32_t)cur;
+                l0 += sel == 0 ? inc : 0u; c0 += sel == 0 ? one : 0u;
+                l1 += sel == 1 ? inc : 0u; c1 += sel == 1 ? one : 0u;
+                l2 += sel == 2 ? inc : 0u; c2 += sel == 2 ? one : 0u;
+                l3 += sel == 3 ? inc : 0u; c3 += sel == 3 ? one : 0u;
+                l4 += sel == 4 ? inc : 0u; c4 += sel == 4 ? one : 0u;
+                pp = p2; blk = blk2;
+            }
         }
         __syncwarp();
         if (lane < bins) offs[lane + 1] = (int)c0;
