@@ -1,15 +1,19 @@
 /*
  * dlx_b200.h - C ABI of the B200 (sm_100a) kernels for Diffulex's decode hot path.
  *
- * Three operators, each the device body of one Python entry point of the reference's
- * diffulex_kernel package:
+ * The operators, each the device body of one Python entry point of the reference's
+ * diffulex_kernel package or of a host loop of its model runner:
  *
  *   dlx_store_kvcache_unified  <- store_kvcache_unified_layout
  *                                 (diffulex_kernel/python/kv_cache_kernels.py:110-124, kernel :11-32)
  *   dlx_load_kvcache           <- load_kvcache (kv_cache_kernels.py:230-279, kernel :127-227)
  *   dlx_decode_attn            <- dllm_flash_attn_decode
  *                                 (diffulex_kernel/python/dllm_flash_attn.py:599-637, kernels :163-536)
+ *                                 and, without a cache, dllm_flash_attn_prefill (:539-596, kernel :23-160)
  *   dlx_store_kvcache_distinct <- store_kvcache_distinct_layout (kv_cache_kernels.py:86-107, kernel :35-83)
+ *   dlx_decode_attn_prepare    <- the per-step lengths and offsets the runner derives for the kernels
+ *                                 (diffulex/strategy/block_diffusion/engine/model_runner.py:125-158)
+ *   dlx_build_slot_mapping     <- the runner's slot-mapping loop (model_runner.py:141-151)
  *
  * Conventions: every pointer is a DEVICE pointer unless stated; strides are in ELEMENTS; all
  * functions only enqueue work on `stream` (a cudaStream_t passed as void*), never synchronise,
