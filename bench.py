@@ -281,11 +281,13 @@ def strong_cfg5(dlx, dp, dev, rank, world, peak):
     q_lens = w_global.new_lens.tolist()
     full = dp.gather_outputs(out, parts, q_lens)
     torch.cuda.synchronize()
-    ea.record()
-    full = dp.gather_outputs(out, parts, q_lens)
-    eb.record()
-    torch.cuda.synchronize()
-    gather_ms = dp.max_over_ranks(ea.elapsed_time(eb), dev)
+    gather_ms = float("inf")
+    for _ in range(3):   # best of three: the first gathers also pay for NCCL's channel set-up
+        ea.record()
+        full = dp.gather_outputs(out, parts, q_lens)
+        eb.record()
+        torch.cuda.synchronize()
+        gather_ms = min(gather_ms, dp.max_over_ranks(ea.elapsed_time(eb), dev))
     bits_sum = lambda t: float(t.contiguous().view(torch.int16).to(torch.int64).sum().item())
     local_sum = bits_sum(out)
     return {
