@@ -114,9 +114,11 @@ def test_split_planning_is_host_only_and_sized_right(lib):
     # long contexts: the persistent tcgen05 kernel balances a long item list by itself (no split) ...
     p = good_params(num_seqs=256, total_q=8192, max_blocks=129)
     assert n(p) == 1
-    # ... but cuts long contexts while there are fewer than two items per SM
+    # ... but cuts long contexts while there are fewer than 1.6 items per schedule bin (here 96 and 116 on 74)
     p = good_params(num_seqs=24, total_q=768, max_blocks=129)
     assert n(p) >= 3
+    assert n(good_params(num_seqs=29, total_q=928, max_blocks=129)) >= 3
+    assert n(good_params(num_seqs=30, total_q=960, max_blocks=129)) == 1
     # the mma.sync kernel launches one CTA per item and keeps cutting long contexts
     p = good_params(num_seqs=256, total_q=8192, max_blocks=129, kernel=1)
     assert n(p) >= 3
