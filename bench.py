@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--no-store-load", action="store_true", help="skip the store / load bandwidth side measurement")
     ap.add_argument("--only-store-load", action="store_true",
                     help="run only the store / load side measurement and print its object (for profiler captures)")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="run only the prefill side measurement and print its object (for profiler captures)")
     ap.add_argument("--store-load-seqs", type=int, default=256,
                     help="sequences of the cfg5-shaped layer used by the store / load measurement (256 = all)")
     return ap.parse_args()
@@ -512,6 +514,9 @@ def main():
 
     if args.only_store_load:
         print(json.dumps(store_load_bandwidth(dlx, dev, peaks()[0], args.store_load_seqs)))
+        return
+    if args.only_prefill:
+        print(json.dumps(prefill_side(dlx, dev)))
         return
 
     # ---- this rank's batch ----
